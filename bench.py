@@ -1,0 +1,515 @@
+"""Benchmark of the B200 GEMM backend; prints ONE JSON line on rank 0.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--workload square8192|rowshard32768] [--quick]
+
+Metric: device-timed TFLOP/s = 2*M*K*N / t (the reference's src/main.py:102).
+
+* N = 1 (default workload ``square8192``): C = A*B with M=K=N=8192, BF16 inputs
+  drawn N(0, 1/sqrt(K)) from a fixed seed, FP32 accumulate and output, through
+  the library's C-ABI (``matmul_launch``, tcgen05 kernel).  A step is one GEMM;
+  W untimed steps, then K steps between CUDA events on the launching stream.
+  A and B (134 MB each) and C (268 MB) are larger than the 126 MB L2, so no
+  flush is needed between steps.  Extra fields report the reference's own
+  timing method (median of 21 CUDA-graph samples of 10 GEMMs after 10 warmups,
+  src/benchmark_backends.py:49-69) for every precision and torch/cuBLAS on the
+  same inputs.
+* N > 1 (default workload ``rowshard32768``): M=K=N=32768 BF16, U[-1,1), A and C
+  row-sharded over the ranks, B broadcast from rank 0, C all-gathered; one
+  process per GPU under torchrun; time = max over ranks.
+* ``--impl reference`` times the reference's CPU path (numpy FP32 GEMM,
+  src/benchmark_backends.py:223-226) on the host cores over row slabs of the
+  same workload; under torchrun only rank 0 runs it.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+PACKAGE = ROOT / "matrix-multiplication_b200"
+ORACLE = ROOT / "oracle"
+sys.path.insert(0, str(PACKAGE))
+
+METRIC = "device-timed TFLOP/s (2MKN/s) per precision at 4096³/8192³, % of B200 peak; 1/2/4/8-GPU"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "sm_max_mhz": 1965.0}
+SM_COUNT = 148
+FFMA_PER_SM_PER_CLK = 128
+
+
+def load_peaks() -> tuple[dict, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        try:
+            return json.loads(path.read_text()), "measured"
+        except ValueError:
+            pass
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def tflops(m, k, n, ms):
+    return 2.0 * m * k * n / (ms * 1e-3) / 1e12
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 100 ms in the background."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.samples = []
+        self.proc = None
+        self.gpu_index = gpu_index
+        self.thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.gpu_index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return self
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.samples.append((time.time(), line.strip()))
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            if self.thread is not None:
+                self.thread.join(timeout=5)
+
+    def summary(self, start: float, stop: float) -> dict:
+        rows = [line for t, line in self.samples if start <= t <= stop]
+        window = "timed region"
+        if not rows:
+            rows = [line for _, line in self.samples]
+            window = "whole run"
+        mhz, max_mhz, power, reasons = [], None, [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in rows:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                mhz.append(float(parts[1]))
+                max_mhz = float(parts[2])
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for name, value in zip(names, parts[5:9]):
+                if value.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": max_mhz,
+                "power_w_max": max(power) if power else None, "reasons": sorted(reasons),
+                "samples": len(mhz), "window": window}
+
+
+# ---------------------------------------------------------------- reference (CPU) arm
+def run_reference_arm(args, rank: int) -> None:
+    if rank != 0:
+        return
+    sys.path.insert(0, str(ORACLE))
+    import numpy as np
+
+    import cpu_backend
+
+    m = k = n = 8192 if args.workload == "square8192" else 32768
+    rows = 512
+    rng = np.random.default_rng(2026)
+    # The reference's CPU path is FP32 only: BF16-representable FP32 inputs.
+    scale = np.float32(k ** -0.5) if args.workload == "square8192" else np.float32(1.0)
+    a = (rng.standard_normal((rows * 2, k), dtype=np.float32) * scale)
+    b = (rng.standard_normal((k, n), dtype=np.float32) * scale)
+    out = np.empty((rows, n), dtype=np.float32)
+    for i in range(args.warmup):
+        cpu_backend.numpy_gemm(a[:rows], b, out)
+    times = []
+    for i in range(args.steps):
+        start = time.perf_counter()
+        cpu_backend.numpy_gemm(a[(i % 2) * rows:(i % 2 + 1) * rows], b, out)
+        times.append(time.perf_counter() - start)
+    total = sum(times)
+    value = 2.0 * rows * k * n * args.steps / total / 1e12
+    cores = cpu_backend.blas_threads()
+    sample = f"{rows} x {k} @ {k} x {n} FP32 numpy row slab per step of the {m}x{k}x{n} workload"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": total / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "strong" if args.gpus > 1 else "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (seeded normal, FP32)",
+        "config": {"workload": f"{args.workload} (CPU row slabs)", "m": m, "k": k, "n": n,
+                   "path": "numpy.matmul FP32 (src/benchmark_backends.py:223-226)"},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def cpu_baseline(seconds: float = 10.0) -> dict:
+    sys.path.insert(0, str(ORACLE))
+    import numpy as np
+
+    import cpu_backend
+
+    k = n = 8192
+    rng = np.random.default_rng(2026)
+    a = rng.standard_normal((1024, k), dtype=np.float32) * np.float32(k ** -0.5)
+    b = rng.standard_normal((k, n), dtype=np.float32) * np.float32(k ** -0.5)
+    result = cpu_backend.time_numpy_slabs(a, b, rows=512, seconds=seconds)
+    return {"value": result["flops"] / result["seconds"] / 1e12, "unit": "TFLOP/s",
+            "cores": cpu_backend.blas_threads(), "kind": "port",
+            "sample": (f"{result['slabs']} row slabs of 512 x 8192 @ 8192 x 8192 FP32 numpy.matmul "
+                       f"({result['seconds']:.1f} s) standing in for the 8192^3 GEMM")}
+
+
+# ---------------------------------------------------------------- single GPU
+def reference_method(run, stream, m, k, n, warmup=10, repeats=21) -> dict:
+    from benchmark_backends import measure_cuda_device
+
+    samples = measure_cuda_device(run, stream, warmup, repeats)
+    median = statistics.median(samples)
+    return {"median_ms": median, "tflops": tflops(m, k, n, median)}
+
+
+def single_gpu(args) -> dict:
+    import numpy as np
+    import torch
+
+    from gpumat import NativeMatmul
+    from precision import INPUT_DTYPES
+
+    peaks, peak_kind = load_peaks()
+    m = k = n = 8192
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    native = NativeMatmul(device=0)
+    stream = torch.cuda.Stream(device=device)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(2026)
+    with torch.cuda.stream(stream):
+        a32 = torch.randn((m, k), generator=gen, device=device) * (k ** -0.5)
+        b32 = torch.randn((k, n), generator=gen, device=device) * (k ** -0.5)
+        a = torch.empty((m, k), dtype=torch.bfloat16, device=device)
+        b = torch.empty((k, n), dtype=torch.bfloat16, device=device)
+        native.convert(a32, a, "bf16")
+        native.convert(b32, b, "bf16")
+        c = torch.empty((m, n), dtype=torch.float32, device=device)
+        run = native.prepare("tcgen05", a, b, c, precision="bf16")
+    stream.synchronize()
+
+    # ---- contract timing: W warm-up steps, then K steps between events.
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            run()
+    stream.synchronize()
+    events = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    with ClockSampler(0) as clocks:
+        time.sleep(0.3)
+        torch.cuda.synchronize()
+        wall0 = time.time()
+        with torch.cuda.stream(stream):
+            events[0].record(stream)
+            for i in range(args.steps):
+                run()
+                events[i + 1].record(stream)
+        stream.synchronize()
+        wall1 = time.time()
+    per_launch = [events[i].elapsed_time(events[i + 1]) for i in range(args.steps)]
+    total_ms = events[0].elapsed_time(events[-1])
+    ms_per_step = total_ms / args.steps
+    value = tflops(m, k, n, ms_per_step)
+    kernel_ms = statistics.mean(per_launch)
+    achieved = tflops(m, k, n, kernel_ms)
+    clock_summary = clocks.summary(wall0, wall1)
+    status = native.device_status()
+
+    # ---- correctness cross-check against torch/cuBLAS on the same inputs (not an oracle).
+    with torch.cuda.stream(stream):
+        ref = torch.mm(a, b, out_dtype=torch.float32)
+    stream.synchronize()
+    check = {"max_abs_diff_vs_torch_cublas": float((ref - c).abs().max().item()),
+             "c_abs_max": float(c.abs().max().item()), "device_status": status}
+    del ref
+
+    # ---- end to end through the public API: pinned FP32 host inputs -> device
+    # conversion -> GEMM -> pinned FP32 host output, every step.
+    host_a = a32.cpu().pin_memory()
+    host_b = b32.cpu().pin_memory()
+    host_c = torch.empty((m, n), dtype=torch.float32).pin_memory()
+    e2e_steps = max(3, min(args.steps, 10))
+
+    def e2e_step():
+        a32.copy_(host_a, non_blocking=True)
+        b32.copy_(host_b, non_blocking=True)
+        native.convert(a32, a, "bf16")
+        native.convert(b32, b, "bf16")
+        run()
+        host_c.copy_(c, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            e2e_step()
+    stream.synchronize()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    wall_e0 = time.perf_counter()
+    with torch.cuda.stream(stream):
+        e_start.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        e_end.record(stream)
+    stream.synchronize()
+    wall_e = (time.perf_counter() - wall_e0) * 1e3 / e2e_steps
+    e2e_ms = e_start.elapsed_time(e_end) / e2e_steps
+    e2e = {"value": tflops(m, k, n, max(e2e_ms, wall_e)), "unit": "TFLOP/s",
+           "h2d_bytes_per_step": 2 * m * k * 4, "d2h_bytes_per_step": m * n * 4,
+           "ms_per_step": max(e2e_ms, wall_e), "steps": e2e_steps,
+           "path": "pinned FP32 host A,B -> H2D -> matmul_convert (RNE to BF16) -> matmul_launch -> D2H FP32 C"}
+    del host_a, host_b, host_c
+
+    # ---- every precision by the reference's own timing method, plus torch/cuBLAS.
+    per_precision = {}
+    cublas = {}
+    if not args.quick:
+        from precision import torch_precision
+
+        for backend, precision in (("tcgen05", "bf16"), ("tcgen05", "fp16"), ("tcgen05", "tf32"), ("ffma", "fp32")):
+            dtype = getattr(torch, INPUT_DTYPES[precision])
+            with torch.cuda.stream(stream):
+                if precision == "bf16":
+                    pa, pb = a, b
+                else:
+                    pa = torch.empty((m, k), dtype=dtype, device=device)
+                    pb = torch.empty((k, n), dtype=dtype, device=device)
+                    native.convert(a32, pa, precision)
+                    native.convert(b32, pb, precision)
+                prun = native.prepare(backend, pa, pb, c, precision=precision)
+            per_precision[precision] = dict(backend=backend, **reference_method(prun, stream, m, k, n))
+            with torch_precision(torch, precision):
+                if precision in ("fp16", "bf16"):
+                    trun = lambda pa=pa, pb=pb: torch.mm(pa, pb, out_dtype=torch.float32, out=c)
+                else:
+                    trun = lambda pa=pa, pb=pb: torch.mm(pa, pb, out=c)
+                cublas[precision] = reference_method(trun, stream, m, k, n)
+            del pa, pb, prun
+        ffma_peak = SM_COUNT * FFMA_PER_SM_PER_CLK * 2 * peaks.get("sm_max_mhz", 1965.0) * 1e6 / 1e12
+        per_precision["fp32"]["ffma_peak_tflops_at_max_clock"] = ffma_peak
+        per_precision["fp32"]["frac_of_ffma_peak"] = per_precision["fp32"]["tflops"] / ffma_peak
+        for precision in ("bf16", "fp16"):
+            per_precision[precision]["frac_of_bf16_peak"] = per_precision[precision]["tflops"] / peaks["bf16_tflops"]
+        per_precision["tf32"]["frac_of_half_bf16_peak"] = per_precision["tf32"]["tflops"] / (peaks["bf16_tflops"] / 2)
+    native.close()
+
+    traffic = None
+    traffic_file = ROOT / "profiles" / "ncu_traffic.json"
+    if traffic_file.exists():
+        traffic = json.loads(traffic_file.read_text()).get("tc_gemm_bf16_8192")
+    peak = peaks["bf16_tflops"]
+    return {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: A, B ~ N(0, 1/sqrt(K)) from a fixed seed, rounded to BF16 (RNE)",
+        "config": {"workload": "gemm_bf16_8192x8192x8192", "m": m, "k": k, "n": n, "precision": "bf16",
+                   "backend": "tcgen05 (matmul_launch impl 7)", "output": "FP32 row-major",
+                   "l2": "inputs larger than L2 (A, B 134 MB each, C 268 MB > 126 MB L2); no flush",
+                   "parallelism": "single GPU"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "traffic": traffic,
+                     "peak_source": f"{peak_kind} bf16_tflops (burst, cuBLAS 8192^3)",
+                     "kernel": "tc_gemm_kernel<BF16>", "kernel_ms": kernel_ms,
+                     "algorithmic_flops_per_launch": 2.0 * m * k * n},
+        "cpu_baseline": cpu_baseline(),
+        "e2e": e2e,
+        "gpu_launches": args.steps,
+        "clocks": clock_summary,
+        "check": check,
+        "per_precision": per_precision,
+        "torch_cublas": cublas,
+    }
+
+
+# ---------------------------------------------------------------- multi GPU
+def multi_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from gpumat import NativeMatmul
+    from sharded import ShardPlan, sharded_step
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    size = args.size or 32768
+    m = k = n = size
+    plan = ShardPlan(m, k, n, world, rank, chunks=args.chunks, gather=args.gather)
+    start, stop = plan.local_rows
+    native = NativeMatmul(device=local_rank)
+    stream = torch.cuda.current_stream(device)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(1000 + rank)
+    a32 = torch.rand((stop - start, k), generator=gen, device=device) * 2 - 1
+    a = torch.empty((stop - start, k), dtype=torch.bfloat16, device=device)
+    native.convert(a32, a, "bf16")
+    del a32
+    b = torch.empty((k, n), dtype=torch.bfloat16, device=device)
+    if rank == 0:
+        gen.manual_seed(7)
+        b32 = torch.rand((k, n), generator=gen, device=device) * 2 - 1
+        native.convert(b32, b, "bf16")
+        del b32
+    c = torch.empty((m, n), dtype=torch.float32, device=device)
+    runs = {}
+
+    def gemm(a_rows, b_full, c_rows):
+        key = (a_rows.data_ptr(), c_rows.data_ptr())
+        if key not in runs:
+            runs[key] = native.prepare("tcgen05", a_rows, b_full, c_rows, precision="bf16")
+        runs[key]()
+
+    for _ in range(args.warmup):
+        sharded_step(plan, a, b, c, gemm)
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        wall0 = time.time()
+        e0.record(stream)
+        for _ in range(args.steps):
+            sharded_step(plan, a, b, c, gemm)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        wall1 = time.time()
+    dist.barrier()
+    ms = torch.tensor([e0.elapsed_time(e1) / args.steps], device=device, dtype=torch.float64)
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms_per_step = float(ms.item())
+    status = native.device_status()
+    clock_summary = clocks.summary(wall0, wall1)
+    native.close()
+    dist.barrier()
+    dist.destroy_process_group()
+    if rank != 0:
+        return None
+    value = tflops(m, k, n, ms_per_step)
+    return {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic: U[-1,1) from fixed seeds, rounded to BF16",
+        "config": {"workload": f"rowshard_bf16_{m}x{k}x{n}", "m": m, "k": k, "n": n, "precision": "bf16",
+                   "parallelism": f"row-sharded A/C over {world} ranks, B broadcast, C "
+                                  f"{'all-gathered' if args.gather == 'all' else 'gathered to rank 0'}",
+                   "chunks": plan.chunk_count, "l2": "inputs larger than L2"},
+        "gpu_launches": args.steps * plan.chunk_count,
+        "clocks": clock_summary, "device_status": status,
+    }
+
+
+def main() -> int:
+    parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=200)
+    parser.add_argument("--warmup", type=int, default=10)
+    parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    parser.add_argument("--workload", choices=("square8192", "rowshard32768"), default=None)
+    parser.add_argument("--size", type=int, default=None, help="override the sharded problem size")
+    parser.add_argument("--chunks", type=int, default=4)
+    parser.add_argument("--gather", choices=("all", "root"), default="all")
+    parser.add_argument("--quick", action="store_true", help="skip the per-precision and cuBLAS tables")
+    args = parser.parse_args()
+    if args.warmup < 3:
+        parser.error("at least 3 warm-up steps")
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.workload is None:
+        args.workload = "square8192" if args.gpus == 1 else "rowshard32768"
+    if args.impl == "reference":
+        run_reference_arm(args, rank)
+        return 0
+    if world > 1 or args.workload == "rowshard32768":
+        if world == 1 and args.gpus > 1:
+            parser.error("--gpus > 1 needs torchrun with one process per GPU")
+        line = multi_gpu(args, rank, world, local_rank) if world > 1 else None
+        if world == 1:
+            line = single_rowshard(args)
+    else:
+        line = single_gpu(args)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def single_rowshard(args) -> dict:
+    """The row-sharded workload on one GPU (its T1): one full GEMM per step."""
+    import torch
+
+    from gpumat import NativeMatmul
+
+    size = args.size or 32768
+    m = k = n = size
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    native = NativeMatmul(device=0)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(1000)
+    a32 = torch.rand((m, k), generator=gen, device=device) * 2 - 1
+    a = torch.empty((m, k), dtype=torch.bfloat16, device=device)
+    native.convert(a32, a, "bf16")
+    del a32
+    b32 = torch.rand((k, n), generator=gen, device=device) * 2 - 1
+    b = torch.empty((k, n), dtype=torch.bfloat16, device=device)
+    native.convert(b32, b, "bf16")
+    del b32
+    c = torch.empty((m, n), dtype=torch.float32, device=device)
+    run = native.prepare("tcgen05", a, b, c, precision="bf16")
+    for _ in range(args.warmup):
+        run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clocks:
+        wall0 = time.time()
+        e0.record()
+        for _ in range(args.steps):
+            run()
+        e1.record()
+        torch.cuda.synchronize()
+        wall1 = time.time()
+    ms_per_step = e0.elapsed_time(e1) / args.steps
+    status = native.device_status()
+    native.close()
+    return {
+        "metric": METRIC, "value": tflops(m, k, n, ms_per_step), "unit": "TFLOP/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: U[-1,1) from fixed seeds, rounded to BF16",
+        "config": {"workload": f"rowshard_bf16_{m}x{k}x{n}", "m": m, "k": k, "n": n, "precision": "bf16",
+                   "parallelism": "single GPU (T1 of the row-sharded workload)", "l2": "inputs larger than L2"},
+        "gpu_launches": args.steps, "clocks": clocks.summary(wall0, wall1), "device_status": status,
+    }
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

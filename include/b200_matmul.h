@@ -1,0 +1,82 @@
+/*
+ * b200_matmul.h -- C-ABI of the B200 (sm_100a) GEMM backend.
+ *
+ * Drop-in replacement for the CUDA library of chudinovAI/matrix-multiplication
+ * (src/matmul.cu, loaded through ctypes by src/gpumat.py).  The five reference
+ * exports keep their names, signatures, ABI version (3) and error convention:
+ * 0 = success, 1 = failure with "operation: detail" written to the caller-owned
+ * buffer `error` of `error_size` bytes.  All matrices are row-major and owned by
+ * the caller: A is m x k, B is k x n (input dtype), C is m x n FP32.  Base
+ * pointers need only element alignment (4 bytes for FP32/TF32, 2 bytes for
+ * FP16/BF16); any m, k, n >= 1 that fit in an int are accepted.
+ *
+ * Implementation ids (the reference's ids 0-6 name kernels this library does
+ * not contain and are rejected with an error):
+ *   7  "tcgen05"  TF32 (1), FP16 (2), BF16 (3): tcgen05.mma with TMEM accumulators
+ *   8  "ffma"     FP32 pedantic (0): register-blocked FFMA, no TF32 anywhere
+ * Precision ids follow src/precision.py:8-10: 0 fp32, 1 tf32, 2 fp16, 3 bf16.
+ */
+#ifndef B200_MATMUL_H
+#define B200_MATMUL_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B200_MATMUL_ABI_VERSION 3
+#define B200_IMPL_TCGEN05 7
+#define B200_IMPL_FFMA 8
+
+/* Replaces matmul_abi_version (src/matmul.cu:213-216); returns 3, the value
+ * src/gpumat.py:31-44 checks. */
+int matmul_abi_version(void);
+
+/* Replaces matmul_kernel_info (src/matmul.cu:218-272): writes a JSON object with
+ * the reference's keys (implementation, precision, tile_m, tile_n, tile_k,
+ * threads, warp_tile_m, warp_tile_n, microtile_m, microtile_n, buffering,
+ * load_method, tensor_cores) plus this library's own geometry keys.  Needs no
+ * GPU. */
+int matmul_kernel_info(int implementation, int precision, char *json, size_t json_size,
+                       char *error, size_t error_size);
+
+/* Replaces matmul_create (src/matmul.cu:274-328): one context per device.  All
+ * per-device setup happens here (kernel attributes, the tensor-map encoder, a
+ * stream-ordered scratch pool); never call it during stream capture.  Returns
+ * NULL on failure and consumes the sticky CUDA error of a failed cudaSetDevice
+ * (src/matmul.cu:280-283). */
+void *matmul_create(int device, char *error, size_t error_size);
+
+/* Replaces matmul_destroy (src/matmul.cu:330-347). */
+int matmul_destroy(void *context, char *error, size_t error_size);
+
+/* Replaces matmul_launch (src/matmul.cu:349-479): C = A * B on `stream`
+ * (a cudaStream_t), asynchronous, CUDA-graph capturable.  TF32 inputs are
+ * rounded to nearest-even before the tensor-core product; unaligned or
+ * TMA-incompatible operands are repacked into stream-ordered scratch first. */
+int matmul_launch(void *context, int implementation, int precision,
+                  const void *a, const void *b, float *c, int m, int k, int n,
+                  void *stream, char *error, size_t error_size);
+
+/* No counterpart in the reference (its end_to_end mode converts with torch's
+ * `.to(dtype)` after the host-to-device copy, src/benchmark_backends.py:295-307).
+ * Converts `count` FP32 values at `src` on `stream` into the input format of
+ * `precision` at `dst`: BF16/FP16 by round-to-nearest-even, TF32 as FP32 words
+ * rounded to 10 fraction bits (ties to even), FP32 as a copy. */
+int matmul_convert(void *context, int precision, const float *src, void *dst, size_t count,
+                   void *stream, char *error, size_t error_size);
+
+/* No counterpart in the reference.  Waits for the device, then reports (and
+ * with `clear` != 0 resets) the library's device status word: 0 when every
+ * kernel finished normally, otherwise bit flags set by a kernel whose bounded
+ * mbarrier wait ran out (1 = operand load, 2 = tensor-core issue,
+ * 4 = epilogue, 8 = teardown drain). */
+int matmul_device_status(void *context, int clear, unsigned int *status,
+                         char *error, size_t error_size);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200_MATMUL_H */

@@ -1,0 +1,511 @@
+// C-ABI of the B200 GEMM backend: context, validation, tensor maps, dispatch.
+//
+// Drop-in for the reference library src/matmul.cu (exports at :213-479): same
+// five symbols, ABI version 3, the same 0/1 return convention with an
+// "operation: detail" message in the caller's buffer, and the same rule that a
+// failed cudaSetDevice leaves no sticky error behind (:280-283).  The kernels
+// behind it are new: tcgen05 tensor-core GEMM (implementation 7) and an FFMA
+// FP32 GEMM (implementation 8).  Declarations: include/b200_matmul.h.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <new>
+
+#include "ffma_gemm.cuh"
+#include "pack.cuh"
+#include "tc_gemm.cuh"
+
+namespace {
+
+using namespace b200;
+
+constexpr int kAbiVersion = 3;
+constexpr int kImplTcgen05 = 7;
+constexpr int kImplFfma = 8;
+constexpr int kPrecFp32 = 0, kPrecTf32 = 1, kPrecFp16 = 2, kPrecBf16 = 3;
+constexpr int kRasterGroupM = 16;
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *,
+                                   CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                   CUtensorMapFloatOOBfill);
+
+struct Context {
+    int device = 0;
+    int major = 0;
+    int minor = 0;
+    int sm_count = 0;
+    EncodeTiledFn encode = nullptr;
+    cudaMemPool_t pool = nullptr;
+};
+
+void clear_error(char *error, size_t error_size)
+{
+    if (error && error_size)
+        error[0] = '\0';
+}
+
+int fail(char *error, size_t error_size, const char *operation, const char *detail)
+{
+    if (error && error_size)
+        std::snprintf(error, error_size, "%s: %s", operation, detail);
+    return 1;
+}
+
+int fail_cuda(char *error, size_t error_size, const char *operation, cudaError_t status)
+{
+    const char *detail = cudaGetErrorString(status);
+    cudaGetLastError();
+    return fail(error, error_size, operation, detail);
+}
+
+bool aligned16(const void *p)
+{
+    return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
+int64_t round_up(int64_t x, int64_t to)
+{
+    return (x + to - 1) / to * to;
+}
+
+bool encode_2d(const Context *ctx, CUtensorMap *map, CUtensorMapDataType type, const void *base, uint64_t inner,
+               uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer)
+{
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {box_inner, box_outer};
+    const cuuint32_t elem_strides[2] = {1, 1};
+    const CUresult r = ctx->encode(map, type, 2, const_cast<void *>(base), dims, strides, box, elem_strides,
+                                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+// Stream-ordered scratch: from the context's pool outside capture, as a graph
+// allocation node inside capture.  Freed on the same stream after use.
+cudaError_t scratch_alloc(Context *ctx, void **ptr, size_t bytes, cudaStream_t stream)
+{
+    cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+    cudaError_t st = cudaStreamIsCapturing(stream, &capture);
+    if (st != cudaSuccess)
+        return st;
+    if (capture == cudaStreamCaptureStatusActive || ctx->pool == nullptr)
+        return cudaMallocAsync(ptr, bytes, stream);
+    return cudaMallocFromPoolAsync(ptr, bytes, ctx->pool, stream);
+}
+
+unsigned int pack_grid_x(int64_t cols)
+{
+    const int64_t blocks = (cols + 255) / 256;
+    return static_cast<unsigned int>(blocks < 64 ? (blocks < 1 ? 1 : blocks) : 64);
+}
+
+unsigned int pack_grid_y(int64_t rows)
+{
+    return static_cast<unsigned int>(rows < 4096 ? rows : 4096);
+}
+
+template <typename T, bool ROUND>
+void launch_pack(const void *src, void *dst, int64_t rows, int64_t cols, int64_t ld, cudaStream_t stream)
+{
+    const dim3 grid(pack_grid_x(ld), pack_grid_y(rows));
+    pack_rows_kernel<T, ROUND><<<grid, 256, 0, stream>>>(static_cast<const T *>(src), static_cast<T *>(dst), rows,
+                                                         cols, ld);
+}
+
+// Prepare one operand for TMA: returns the pointer and leading dimension to use.
+void prepare_operand(int prec, const void *src, int64_t rows, int64_t cols, bool direct, void *scratch,
+                     int64_t ld, const Context *ctx, cudaStream_t stream)
+{
+    if (direct)
+        return;
+    if (prec == kPrecTf32) {
+        if (ld == cols && aligned16(src)) {
+            const int64_t count4 = rows * cols / 4;
+            const int64_t blocks = (count4 + 255) / 256;
+            const unsigned int grid =
+                static_cast<unsigned int>(blocks < 8LL * ctx->sm_count ? (blocks < 1 ? 1 : blocks)
+                                                                       : 8LL * ctx->sm_count);
+            round_tf32_vec_kernel<<<grid, 256, 0, stream>>>(static_cast<const float4 *>(src),
+                                                            static_cast<float4 *>(scratch), count4);
+        } else {
+            launch_pack<float, true>(src, scratch, rows, cols, ld, stream);
+        }
+    } else if (prec == kPrecBf16) {
+        launch_pack<__nv_bfloat16, false>(src, scratch, rows, cols, ld, stream);
+    } else {
+        launch_pack<__half, false>(src, scratch, rows, cols, ld, stream);
+    }
+}
+
+template <int FMT>
+cudaError_t launch_tc_kernel(const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &mc,
+                             const TcParams &params, int grid, cudaStream_t stream)
+{
+    tc_gemm_kernel<FMT><<<grid, TC_THREADS, TC_SMEM_BYTES, stream>>>(ma, mb, mc, params);
+    return cudaGetLastError();
+}
+
+int launch_tcgen05(Context *ctx, int prec, const void *a, const void *b, float *c, int m, int k, int n,
+                   cudaStream_t stream, char *error, size_t error_size)
+{
+    const int elem = prec == kPrecTf32 ? 4 : 2;
+    const int64_t align_elems = 16 / elem;
+    // TMA needs 16-byte aligned bases and row pitches; TF32 always needs rounding.
+    const bool a_direct = prec != kPrecTf32 && aligned16(a) && (static_cast<int64_t>(k) * elem) % 16 == 0;
+    const bool b_direct = prec != kPrecTf32 && aligned16(b) && (static_cast<int64_t>(n) * elem) % 16 == 0;
+    const int64_t lda = a_direct ? k : round_up(k, align_elems);
+    const int64_t ldb = b_direct ? n : round_up(n, align_elems);
+    const size_t a_bytes = a_direct ? 0 : static_cast<size_t>(round_up(static_cast<int64_t>(m) * lda * elem, 256));
+    const size_t b_bytes = b_direct ? 0 : static_cast<size_t>(round_up(static_cast<int64_t>(k) * ldb * elem, 256));
+
+    void *scratch = nullptr;
+    if (a_bytes + b_bytes) {
+        const cudaError_t st = scratch_alloc(ctx, &scratch, a_bytes + b_bytes, stream);
+        if (st != cudaSuccess)
+            return fail_cuda(error, error_size, "matmul_launch: scratch allocation", st);
+    }
+    const void *a_op = a_direct ? a : scratch;
+    const void *b_op = b_direct ? b : static_cast<uint8_t *>(scratch) + a_bytes;
+    prepare_operand(prec, a, m, k, a_direct, const_cast<void *>(a_op), lda, ctx, stream);
+    prepare_operand(prec, b, k, n, b_direct, const_cast<void *>(b_op), ldb, ctx, stream);
+
+    const CUtensorMapDataType type = prec == kPrecTf32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                     : prec == kPrecBf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                         : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const uint32_t bk = TC_ROW_BYTES / elem;
+    alignas(64) CUtensorMap map_a, map_b, map_c;
+    std::memset(&map_c, 0, sizeof(map_c));
+    bool ok = encode_2d(ctx, &map_a, type, a_op, static_cast<uint64_t>(k), static_cast<uint64_t>(m),
+                        static_cast<uint64_t>(lda) * elem, bk, TC_BM);
+    ok = ok && encode_2d(ctx, &map_b, type, b_op, static_cast<uint64_t>(n), static_cast<uint64_t>(k),
+                         static_cast<uint64_t>(ldb) * elem, TC_ROW_BYTES / elem, bk);
+    const bool c_direct = !(aligned16(c) && n % 4 == 0);
+    if (ok && !c_direct)
+        ok = encode_2d(ctx, &map_c, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, c, static_cast<uint64_t>(n),
+                       static_cast<uint64_t>(m), static_cast<uint64_t>(n) * 4, 32, 32);
+    if (!ok) {
+        if (scratch)
+            cudaFreeAsync(scratch, stream);
+        cudaGetLastError();
+        return fail(error, error_size, "matmul_launch", "cuTensorMapEncodeTiled rejected an operand");
+    }
+
+    TcParams params{};
+    params.m = m;
+    params.n = n;
+    params.k = k;
+    params.num_m_blocks = (m + TC_BM - 1) / TC_BM;
+    params.num_n_blocks = (n + TC_BN - 1) / TC_BN;
+    params.num_k_blocks = static_cast<int>((static_cast<int64_t>(k) + bk - 1) / bk);
+    const int64_t tiles = static_cast<int64_t>(params.num_m_blocks) * params.num_n_blocks;
+    if (tiles > 0x7fffffff) {
+        if (scratch)
+            cudaFreeAsync(scratch, stream);
+        return fail(error, error_size, "matmul_launch", "too many output tiles");
+    }
+    params.num_tiles = static_cast<int>(tiles);
+    params.group_m = kRasterGroupM;
+    params.c = c;
+    params.c_direct = c_direct ? 1 : 0;
+    const int grid = static_cast<int>(tiles < ctx->sm_count ? tiles : ctx->sm_count);
+
+    cudaError_t st;
+    if (prec == kPrecTf32)
+        st = launch_tc_kernel<kFmtTF32>(map_a, map_b, map_c, params, grid, stream);
+    else if (prec == kPrecBf16)
+        st = launch_tc_kernel<kFmtBF16>(map_a, map_b, map_c, params, grid, stream);
+    else
+        st = launch_tc_kernel<kFmtF16>(map_a, map_b, map_c, params, grid, stream);
+    if (scratch)
+        cudaFreeAsync(scratch, stream);
+    if (st != cudaSuccess)
+        return fail(error, error_size, "kernel launch", cudaGetErrorString(st));
+    return 0;
+}
+
+template <bool VA, bool VB, bool VC>
+void launch_ffma_kernel(const float *a, const float *b, float *c, int m, int k, int n, cudaStream_t stream)
+{
+    const int64_t gx = (static_cast<int64_t>(n) + FF_BN - 1) / FF_BN;
+    const int64_t gy = (static_cast<int64_t>(m) + FF_BM - 1) / FF_BM;
+    const dim3 grid(static_cast<unsigned int>(gx < 65535 ? gx : 65535),
+                    static_cast<unsigned int>(gy < 65535 ? gy : 65535));
+    ffma_gemm_kernel<VA, VB, VC><<<grid, FF_THREADS, 0, stream>>>(a, b, c, m, n, k);
+}
+
+int launch_ffma(const float *a, const float *b, float *c, int m, int k, int n, cudaStream_t stream, char *error,
+                size_t error_size)
+{
+    const bool va = aligned16(a) && k % 4 == 0;
+    const bool vb = aligned16(b) && n % 4 == 0;
+    const bool vc = aligned16(c) && n % 4 == 0;
+    if (va && vb && vc)
+        launch_ffma_kernel<true, true, true>(a, b, c, m, k, n, stream);
+    else if (va && vb)
+        launch_ffma_kernel<true, true, false>(a, b, c, m, k, n, stream);
+    else
+        launch_ffma_kernel<false, false, false>(a, b, c, m, k, n, stream);
+    const cudaError_t st = cudaGetLastError();
+    if (st != cudaSuccess)
+        return fail(error, error_size, "kernel launch", cudaGetErrorString(st));
+    return 0;
+}
+
+const char *kPrecisionNames[] = {"fp32", "tf32", "fp16", "bf16"};
+
+bool supported(int implementation, int precision)
+{
+    if (implementation == kImplTcgen05)
+        return precision == kPrecTf32 || precision == kPrecFp16 || precision == kPrecBf16;
+    if (implementation == kImplFfma)
+        return precision == kPrecFp32;
+    return false;
+}
+
+int check_ids(int implementation, int precision, const char *op, char *error, size_t error_size)
+{
+    if (precision < 0 || precision > 3)
+        return fail(error, error_size, op, "unknown precision");
+    if (implementation >= 0 && implementation <= 6)
+        return fail(error, error_size, op,
+                    "implementations 0-6 (the sm_80 reference kernels and cuBLAS) are not part of this "
+                    "library; use 7 (tcgen05) or 8 (ffma)");
+    if (implementation != kImplTcgen05 && implementation != kImplFfma)
+        return fail(error, error_size, op, "unknown implementation");
+    if (!supported(implementation, precision))
+        return fail(error, error_size, op, "unsupported implementation and precision");
+    return 0;
+}
+
+} // namespace
+
+extern "C" int matmul_abi_version()
+{
+    return kAbiVersion;
+}
+
+extern "C" int matmul_kernel_info(int implementation, int precision, char *json, size_t json_size, char *error,
+                                  size_t error_size)
+{
+    clear_error(error, error_size);
+    if (!json || !json_size)
+        return fail(error, error_size, "matmul_kernel_info", "JSON buffer is null or empty");
+    json[0] = '\0';
+    if (check_ids(implementation, precision, "matmul_kernel_info", error, error_size))
+        return 1;
+    int written;
+    if (implementation == kImplTcgen05) {
+        const int elem = precision == kPrecTf32 ? 4 : 2;
+        written = std::snprintf(
+            json, json_size,
+            "{\"implementation\":\"tcgen05\",\"precision\":\"%s\",\"tile_m\":%d,\"tile_n\":%d,"
+            "\"tile_k\":%d,\"threads\":%d,\"warp_tile_m\":%d,\"warp_tile_n\":%d,\"microtile_m\":%d,"
+            "\"microtile_n\":%d,\"buffering\":%d,\"load_method\":\"tma_sw128\",\"tensor_cores\":true,"
+            "\"mma\":\"tcgen05.mma.cta_group::1.kind::%s\",\"mma_shape\":[%d,%d,%d],"
+            "\"accumulator\":\"tmem_fp32\",\"tmem_columns\":%u,\"accumulator_buffers\":2,"
+            "\"warp_roles\":{\"tma\":1,\"mma\":1,\"epilogue\":4},\"schedule\":\"persistent\","
+            "\"raster_group_m\":%d,\"epilogue\":\"tmem_ld_smem_tma_store\","
+            "\"input_rounding\":\"%s\"}",
+            kPrecisionNames[precision], TC_BM, TC_BN, TC_ROW_BYTES / elem, TC_THREADS, TC_BM, TC_BN, TC_BM,
+            TC_BN, TC_STAGES, precision == kPrecTf32 ? "tf32" : "f16", TC_BM, TC_BN, 32 / elem,
+            TC_TMEM_COLUMNS, kRasterGroupM, precision == kPrecTf32 ? "rne_prepass" : "none");
+    } else {
+        written = std::snprintf(
+            json, json_size,
+            "{\"implementation\":\"ffma\",\"precision\":\"fp32\",\"tile_m\":%d,\"tile_n\":%d,"
+            "\"tile_k\":%d,\"threads\":%d,\"warp_tile_m\":%d,\"warp_tile_n\":%d,\"microtile_m\":8,"
+            "\"microtile_n\":8,\"buffering\":2,\"load_method\":\"float4_masked_register_prefetch\","
+            "\"tensor_cores\":false,\"blocks_per_sm\":2}",
+            FF_BM, FF_BN, FF_BK, FF_THREADS, 16, 128);
+    }
+    if (written < 0 || static_cast<size_t>(written) >= json_size) {
+        json[0] = '\0';
+        return fail(error, error_size, "matmul_kernel_info", "JSON buffer too small");
+    }
+    return 0;
+}
+
+extern "C" void *matmul_create(int device, char *error, size_t error_size)
+{
+    clear_error(error, error_size);
+    cudaError_t st = cudaSetDevice(device);
+    if (st != cudaSuccess) {
+        fail_cuda(error, error_size, "cudaSetDevice", st);
+        return nullptr;
+    }
+    int major = 0, minor = 0, sms = 0;
+    st = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+    if (st == cudaSuccess)
+        st = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device);
+    if (st == cudaSuccess)
+        st = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    if (st != cudaSuccess) {
+        fail_cuda(error, error_size, "cudaDeviceGetAttribute", st);
+        return nullptr;
+    }
+    if (major != 10 || minor != 0) {
+        char detail[160];
+        std::snprintf(detail, sizeof(detail),
+                      "device %d has compute capability %d.%d; this library contains sm_100a code only", device,
+                      major, minor);
+        fail(error, error_size, "matmul_create", detail);
+        return nullptr;
+    }
+
+    Context *ctx = new (std::nothrow) Context{};
+    if (!ctx) {
+        fail(error, error_size, "matmul_create", "could not allocate context");
+        return nullptr;
+    }
+    ctx->device = device;
+    ctx->major = major;
+    ctx->minor = minor;
+    ctx->sm_count = sms;
+
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult query{};
+    st = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &query);
+    if (st != cudaSuccess || query != cudaDriverEntryPointSuccess || !fn) {
+        delete ctx;
+        if (st != cudaSuccess)
+            fail_cuda(error, error_size, "cudaGetDriverEntryPoint", st);
+        else
+            fail(error, error_size, "cudaGetDriverEntryPoint", "cuTensorMapEncodeTiled not found");
+        return nullptr;
+    }
+    ctx->encode = reinterpret_cast<EncodeTiledFn>(fn);
+
+    const void *tc_kernels[] = {reinterpret_cast<const void *>(&tc_gemm_kernel<kFmtF16>),
+                                reinterpret_cast<const void *>(&tc_gemm_kernel<kFmtBF16>),
+                                reinterpret_cast<const void *>(&tc_gemm_kernel<kFmtTF32>)};
+    for (const void *kernel : tc_kernels) {
+        st = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM_BYTES);
+        if (st != cudaSuccess) {
+            delete ctx;
+            fail_cuda(error, error_size, "cudaFuncSetAttribute", st);
+            return nullptr;
+        }
+    }
+
+    cudaMemPoolProps props{};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = device;
+    st = cudaMemPoolCreate(&ctx->pool, &props);
+    if (st == cudaSuccess) {
+        uint64_t keep = UINT64_MAX;
+        cudaMemPoolSetAttribute(ctx->pool, cudaMemPoolAttrReleaseThreshold, &keep);
+    } else {
+        ctx->pool = nullptr;
+        cudaGetLastError();
+    }
+    return ctx;
+}
+
+extern "C" int matmul_destroy(void *opaque, char *error, size_t error_size)
+{
+    clear_error(error, error_size);
+    if (!opaque)
+        return fail(error, error_size, "matmul_destroy", "context is null");
+    Context *ctx = static_cast<Context *>(opaque);
+    const cudaError_t st = cudaSetDevice(ctx->device);
+    if (st != cudaSuccess)
+        return fail_cuda(error, error_size, "cudaSetDevice", st);
+    if (ctx->pool) {
+        // Outstanding stream-ordered frees must retire before the pool goes away.
+        cudaDeviceSynchronize();
+        cudaMemPoolDestroy(ctx->pool);
+        cudaGetLastError();
+    }
+    delete ctx;
+    return 0;
+}
+
+extern "C" int matmul_launch(void *opaque, int implementation, int precision, const void *a, const void *b,
+                             float *c, int m, int k, int n, void *stream, char *error, size_t error_size)
+{
+    clear_error(error, error_size);
+    if (!opaque)
+        return fail(error, error_size, "matmul_launch", "context is null");
+    if (!a || !b || !c)
+        return fail(error, error_size, "matmul_launch", "matrix pointer is null");
+    if (m <= 0 || k <= 0 || n <= 0)
+        return fail(error, error_size, "matmul_launch", "dimensions must be positive");
+    if (check_ids(implementation, precision, "matmul_launch", error, error_size))
+        return 1;
+    const size_t elem = precision == kPrecFp16 || precision == kPrecBf16 ? 2 : 4;
+    if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b)) % elem ||
+        reinterpret_cast<uintptr_t>(c) % 4)
+        return fail(error, error_size, "matmul_launch", "matrix pointer is not aligned to its element size");
+    Context *ctx = static_cast<Context *>(opaque);
+    const cudaError_t st = cudaSetDevice(ctx->device);
+    if (st != cudaSuccess)
+        return fail_cuda(error, error_size, "cudaSetDevice", st);
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (implementation == kImplFfma)
+        return launch_ffma(static_cast<const float *>(a), static_cast<const float *>(b), c, m, k, n, s, error,
+                           error_size);
+    return launch_tcgen05(ctx, precision, a, b, c, m, k, n, s, error, error_size);
+}
+
+extern "C" int matmul_convert(void *opaque, int precision, const float *src, void *dst, size_t count, void *stream,
+                              char *error, size_t error_size)
+{
+    clear_error(error, error_size);
+    if (!opaque)
+        return fail(error, error_size, "matmul_convert", "context is null");
+    if (precision < 0 || precision > 3)
+        return fail(error, error_size, "matmul_convert", "unknown precision");
+    if (!src || !dst)
+        return fail(error, error_size, "matmul_convert", "pointer is null");
+    if (count == 0)
+        return 0;
+    Context *ctx = static_cast<Context *>(opaque);
+    cudaError_t st = cudaSetDevice(ctx->device);
+    if (st != cudaSuccess)
+        return fail_cuda(error, error_size, "cudaSetDevice", st);
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int64_t n = static_cast<int64_t>(count);
+    const int64_t blocks = (n + 255) / 256;
+    const unsigned int grid = static_cast<unsigned int>(blocks < 16LL * ctx->sm_count ? blocks : 16LL * ctx->sm_count);
+    if (precision == kPrecFp32)
+        st = cudaMemcpyAsync(dst, src, count * sizeof(float), cudaMemcpyDeviceToDevice, s);
+    else if (precision == kPrecTf32)
+        convert_f32_kernel<float><<<grid, 256, 0, s>>>(src, static_cast<float *>(dst), n);
+    else if (precision == kPrecBf16)
+        convert_f32_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(src, static_cast<__nv_bfloat16 *>(dst), n);
+    else
+        convert_f32_kernel<__half><<<grid, 256, 0, s>>>(src, static_cast<__half *>(dst), n);
+    if (st == cudaSuccess)
+        st = cudaGetLastError();
+    if (st != cudaSuccess)
+        return fail(error, error_size, "matmul_convert", cudaGetErrorString(st));
+    return 0;
+}
+
+extern "C" int matmul_device_status(void *opaque, int clear, unsigned int *status, char *error, size_t error_size)
+{
+    clear_error(error, error_size);
+    if (!opaque)
+        return fail(error, error_size, "matmul_device_status", "context is null");
+    if (!status)
+        return fail(error, error_size, "matmul_device_status", "status pointer is null");
+    Context *ctx = static_cast<Context *>(opaque);
+    cudaError_t st = cudaSetDevice(ctx->device);
+    if (st == cudaSuccess)
+        st = cudaDeviceSynchronize();
+    if (st == cudaSuccess)
+        st = cudaMemcpyFromSymbol(status, g_device_status, sizeof(unsigned int));
+    if (st == cudaSuccess && clear) {
+        const unsigned int zero = 0;
+        st = cudaMemcpyToSymbol(g_device_status, &zero, sizeof(unsigned int));
+    }
+    if (st != cudaSuccess)
+        return fail_cuda(error, error_size, "matmul_device_status", st);
+    return 0;
+}

@@ -1,0 +1,326 @@
+// Persistent warp-specialised tcgen05 GEMM: C (FP32, m x n) = A (m x k) * B (k x n),
+// row-major, TF32 / FP16 / BF16 inputs, FP32 accumulation in tensor memory.
+//
+// Replaces the reference's matmul_wmma<T,BK> (src/matmul_custom.cuh:169-235),
+// which staged scalars through shared memory into mma.sync fragments.  Here:
+//
+//   warp 0      TMA producer: one elected lane streams A (128 x 128 B) and
+//               B (128 B-wide column blocks) boxes into a 4-stage ring with
+//               128-byte swizzle, signalling a "full" mbarrier per stage.
+//   warp 1      TMEM owner + MMA issuer: allocates 512 TMEM columns (two
+//               128 x 256 FP32 accumulators) and one lane issues
+//               tcgen05.mma (M=128, N=256, K=32 bytes) per K slice; a
+//               tcgen05.commit frees each smem stage and publishes each
+//               finished accumulator.
+//   warps 2-5   epilogue: tcgen05.ld 32 columns at a time, stage them in a
+//               swizzled 32 x 32 FP32 box per warp and TMA-store them (or, when C
+//               is not TMA-compatible, store directly with bounds checks).
+//               Runs one tile behind the MMA thanks to the two accumulators.
+//
+// A is K-major in shared memory; B stays row-major (N contiguous), i.e. the
+// MN-major operand form of the instruction descriptor, so neither operand is
+// transposed in memory.  Tiles are visited persistently (tile += gridDim.x)
+// in groups of `group_m` M-blocks so that concurrently running CTAs share A
+// and B panels in L2.
+#pragma once
+
+#include <cuda.h>
+#include <cstdint>
+
+#include "ptx.cuh"
+
+namespace b200 {
+
+// Device status word: bit flags set by a kernel whose bounded wait gave up.
+__device__ unsigned int g_device_status;
+
+enum : unsigned int {
+    kStatusLoadTimeout = 1u,
+    kStatusMmaTimeout = 2u,
+    kStatusEpilogueTimeout = 4u,
+    kStatusDrainTimeout = 8u,
+};
+
+__device__ __forceinline__ void report_status(unsigned int flag)
+{
+    atomicOr(&g_device_status, flag);
+}
+
+enum TcFormat : int { kFmtF16 = 0, kFmtBF16 = 1, kFmtTF32 = 2 };
+
+constexpr int TC_BM = 128;                  // rows per tile (TMEM lanes)
+constexpr int TC_BN = 256;                  // columns per tile (TMEM columns per accumulator)
+constexpr int TC_STAGES = 4;                // smem ring depth
+constexpr int TC_THREADS = 192;             // 6 warps
+constexpr int TC_ROW_BYTES = 128;           // one swizzle row = K-slice depth of a stage
+constexpr int TC_A_STAGE = TC_BM * TC_ROW_BYTES;   // 16 KB
+constexpr int TC_B_STAGE = TC_BN * TC_ROW_BYTES;   // 32 KB (BK rows x BN elements)
+constexpr int TC_EPI_BOX = 32 * 32 * 4;            // 32 rows x 32 FP32 columns
+constexpr int TC_EPI_BYTES = 4 * 2 * TC_EPI_BOX;   // 4 warps, double buffered
+constexpr int TC_BAR_BYTES = 256;
+constexpr int TC_SMEM_BYTES =
+    1024 /* alignment slack */ + TC_STAGES * (TC_A_STAGE + TC_B_STAGE) + TC_EPI_BYTES + TC_BAR_BYTES;
+constexpr uint32_t TC_TMEM_COLUMNS = 2 * TC_BN;
+
+struct TcParams {
+    int m, n, k;
+    int num_m_blocks, num_n_blocks, num_k_blocks;
+    int num_tiles;
+    int group_m;     // M-blocks per raster group
+    float *c;        // output (direct-store epilogue only)
+    int c_direct;    // 1 when C cannot be written by TMA
+};
+
+// Instruction descriptor (kind::f16 / kind::tf32): FP32 accumulator (bits 4-5 = 1),
+// A/B formats (bits 7-9, 10-12), A K-major (bit 15 = 0), B MN-major (bit 16 = 1),
+// N >> 3 in bits 17-22, M >> 4 in bits 24-28.
+__host__ __device__ constexpr uint32_t tc_instr_desc(int fmt)
+{
+    return (1u << 4) | (static_cast<uint32_t>(fmt) << 7) | (static_cast<uint32_t>(fmt) << 10) |
+           (0u << 15) | (1u << 16) | (static_cast<uint32_t>(TC_BN >> 3) << 17) |
+           (static_cast<uint32_t>(TC_BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void tc_tile_coords(int tile, const TcParams &p, int &mb, int &nb)
+{
+    const int per_group = p.group_m * p.num_n_blocks;
+    const int group = tile / per_group;
+    const int first_m = group * p.group_m;
+    const int rows = min(p.num_m_blocks - first_m, p.group_m);
+    const int local = tile - group * per_group;
+    mb = first_m + local % rows;
+    nb = local / rows;
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+               const __grid_constant__ CUtensorMap map_c, const TcParams p)
+{
+    constexpr bool kTF32 = FMT == kFmtTF32;
+    constexpr int kElem = kTF32 ? 4 : 2;
+    constexpr int kBK = TC_ROW_BYTES / kElem;          // K elements per stage (64 or 32)
+    constexpr int kMmaK = 32 / kElem;                  // K per instruction (16 or 8)
+    constexpr int kMmasPerStage = kBK / kMmaK;         // 4
+    constexpr int kNB = TC_ROW_BYTES / kElem;          // B box width in elements (64 or 32)
+    constexpr int kBBoxes = TC_BN / kNB;               // 4 or 8
+    constexpr uint32_t kBBoxBytes = kBK * TC_ROW_BYTES;  // bytes per B column block
+    constexpr uint32_t kIdesc = tc_instr_desc(FMT);
+
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_addr(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    const uint32_t s_a = base;
+    const uint32_t s_b = s_a + TC_STAGES * TC_A_STAGE;
+    const uint32_t s_epi = s_b + TC_STAGES * TC_B_STAGE;
+    const uint32_t s_bar = s_epi + TC_EPI_BYTES;
+    auto full_bar = [&](int s) { return s_bar + 8u * s; };
+    auto empty_bar = [&](int s) { return s_bar + 8u * (TC_STAGES + s); };
+    auto accf_bar = [&](int i) { return s_bar + 8u * (2 * TC_STAGES + i); };
+    auto acce_bar = [&](int i) { return s_bar + 8u * (2 * TC_STAGES + 2 + i); };
+    const uint32_t drain_bar = s_bar + 8u * (2 * TC_STAGES + 4);
+    const uint32_t tmem_slot = s_bar + 8u * (2 * TC_STAGES + 5);
+    uint32_t *tmem_slot_ptr = reinterpret_cast<uint32_t *>(smem_raw + (tmem_slot - raw));
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < TC_STAGES; ++s) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(accf_bar(i), 1);
+            mbar_init(acce_bar(i), 128);
+        }
+        mbar_init(drain_bar, 1);
+        fence_mbarrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_map(&map_a);
+        tma_prefetch_map(&map_b);
+        if (!p.c_direct)
+            tma_prefetch_map(&map_c);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, TC_TMEM_COLUMNS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t *>(tmem_slot_ptr);
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t filled = 0, fill_parity = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+                int mb, nb;
+                tc_tile_coords(tile, p, mb, nb);
+                for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+                    if (!mbar_wait(empty_bar(stage), phase ^ 1u)) {
+                        report_status(kStatusLoadTimeout);
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(full_bar(stage), TC_A_STAGE + TC_B_STAGE);
+                    tma_load_2d(s_a + stage * TC_A_STAGE, &map_a, full_bar(stage), kb * kBK, mb * TC_BM);
+#pragma unroll
+                    for (int j = 0; j < kBBoxes; ++j)
+                        tma_load_2d(s_b + stage * TC_B_STAGE + j * kBBoxBytes, &map_b, full_bar(stage),
+                                    nb * TC_BN + j * kNB, kb * kBK);
+                    filled |= 1u << stage;
+                    fill_parity = (fill_parity & ~(1u << stage)) | (phase << stage);
+                    if (++stage == TC_STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            // Let every issued copy land before the CTA can exit.
+            for (int s = 0; s < TC_STAGES; ++s)
+                if ((filled >> s) & 1u)
+                    if (!mbar_wait(full_bar(s), (fill_parity >> s) & 1u))
+                        report_status(kStatusDrainTimeout);
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+                if (!mbar_wait(acce_bar(acc), acc_phase ^ 1u)) {
+                    report_status(kStatusMmaTimeout);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * TC_BN);
+                for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+                    if (!mbar_wait(full_bar(stage), phase)) {
+                        report_status(kStatusMmaTimeout);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_stage = s_a + stage * TC_A_STAGE;
+                    const uint32_t b_stage = s_b + stage * TC_B_STAGE;
+#pragma unroll
+                    for (int kk = 0; kk < kMmasPerStage; ++kk) {
+                        // A: K-major SW128, K slice kk starts 32 bytes further inside each row.
+                        const uint64_t a_desc = smem_desc_sw128(a_stage + kk * 32, 16, 1024);
+                        // B: MN-major SW128, K slice kk starts kMmaK rows (x 128 B) further;
+                        // column blocks are kBBoxBytes apart.
+                        const uint64_t b_desc =
+                            smem_desc_sw128(b_stage + kk * kMmaK * TC_ROW_BYTES, kBBoxBytes, 1024);
+                        tc_mma<kTF32>(d_tmem, a_desc, b_desc, kIdesc, (kb | kk) != 0 ? 1u : 0u);
+                    }
+                    tc_commit(empty_bar(stage));
+                    if (++stage == TC_STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok)
+                    break;
+                tc_commit(accf_bar(acc));
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+            }
+            // Every MMA issued above completes before TMEM is released.
+            tc_commit(drain_bar);
+            if (!mbar_wait(drain_bar, 0))
+                report_status(kStatusDrainTimeout);
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------------------ epilogue
+        const int quarter = warp & 3;               // TMEM lanes 32*quarter .. +31
+        const uint32_t box0 = s_epi + (warp - 2) * 2 * TC_EPI_BOX;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        uint32_t stores = 0;
+        for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+            int mb, nb;
+            tc_tile_coords(tile, p, mb, nb);
+            int ok = 1;
+            if (lane == 0)
+                ok = mbar_wait(accf_bar(acc), acc_phase) ? 1 : 0;
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) {
+                if (lane == 0)
+                    report_status(kStatusEpilogueTimeout);
+                break;
+            }
+            tc_fence_after();
+            const int row0 = mb * TC_BM + quarter * 32;
+            const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                                   static_cast<uint32_t>(acc * TC_BN);
+#pragma unroll 1
+            for (int chunk = 0; chunk < TC_BN / 32; ++chunk) {
+                uint32_t v[32];
+                tmem_load_32cols(t_row + chunk * 32, v);
+                if (chunk == TC_BN / 32 - 1) {
+                    tc_fence_before();
+                    mbar_arrive(acce_bar(acc));
+                }
+                const int col0 = nb * TC_BN + chunk * 32;
+                if (col0 >= p.n || row0 >= p.m)
+                    continue;
+                if (!p.c_direct) {
+                    const uint32_t box = box0 + (stores & 1u) * TC_EPI_BOX;
+                    if (lane == 0)
+                        bulk_wait_group_read<1>();
+                    __syncwarp();
+                    const uint32_t row_addr = box + lane * 128;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        st_shared_v4(row_addr + ((j ^ (lane & 7)) << 4), v[4 * j], v[4 * j + 1], v[4 * j + 2],
+                                     v[4 * j + 3]);
+                    fence_proxy_async_shared();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&map_c, box, col0, row0);
+                        bulk_commit_group();
+                    }
+                    ++stores;
+                } else {
+                    const int row = row0 + lane;
+                    if (row < p.m) {
+                        float *dst = p.c + static_cast<size_t>(row) * p.n;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (col0 + j < p.n)
+                                dst[col0 + j] = __uint_as_float(v[j]);
+                    }
+                }
+            }
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1u;
+            }
+        }
+        if (lane == 0)
+            bulk_wait_group<0>();
+        __syncwarp();
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, TC_TMEM_COLUMNS);
+    }
+}
+
+} // namespace b200

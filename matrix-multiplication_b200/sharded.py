@@ -1,0 +1,120 @@
+"""Row-sharded multi-GPU GEMM: C = A * B over P ranks of one node.
+
+The reference is single-device (src/benchmark_backends.py selects one
+``--device``); this module is the multi-GPU layer of the B200 backend:
+
+* rank r owns rows ``shard_rows(M, P, r)`` of A and C (contiguous row blocks);
+* B (K x N) lives on rank 0 and is broadcast to every rank (NCCL over NVLink);
+* each rank computes its C rows with the library's tcgen05 GEMM, one row
+  chunk at a time, and every finished chunk is exchanged with grouped
+  point-to-point transfers straight into each peer's full C (all-gather) or
+  into rank 0's C only (gather to root), so the exchange of chunk i overlaps
+  the GEMM of chunk i+1.  No kernel reads peer memory.
+
+Collectives are issued through ``torch.distributed`` (one process per GPU);
+the host-side plan (row ranges, chunking, peer lists) is independent of the
+backend and is tested with ``gloo`` ranks on CPU.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable
+
+import torch
+import torch.distributed as dist
+
+
+def shard_rows(m: int, world: int, rank: int) -> tuple[int, int]:
+    """Row range [start, stop) of rank ``rank``: contiguous, sizes differ by at most one."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError("rank must be in [0, world)")
+    base, extra = divmod(m, world)
+    start = rank * base + min(rank, extra)
+    stop = start + base + (1 if rank < extra else 0)
+    return start, stop
+
+
+def chunk_rows(rows: int, chunks: int) -> list[tuple[int, int]]:
+    """Split ``rows`` local rows into at most ``chunks`` non-empty contiguous ranges."""
+    chunks = max(1, min(chunks, rows)) if rows > 0 else 0
+    return [shard_rows(rows, chunks, i) for i in range(chunks)]
+
+
+@dataclass
+class ShardPlan:
+    m: int
+    k: int
+    n: int
+    world: int
+    rank: int
+    chunks: int
+    gather: str = "all"           # "all": every rank gets C; "root": rank 0 gets C
+
+    def __post_init__(self):
+        if self.gather not in ("all", "root"):
+            raise ValueError("gather must be 'all' or 'root'")
+        self.rows = [shard_rows(self.m, self.world, r) for r in range(self.world)]
+        # Every rank splits its rows into the same number of chunks so that chunk i
+        # is exchanged in the same grouped call on every rank.
+        min_rows = min(stop - start for start, stop in self.rows)
+        self.chunk_count = max(1, min(self.chunks, min_rows)) if min_rows > 0 else 1
+        self.chunk_ranges = [chunk_rows(stop - start, self.chunk_count) for start, stop in self.rows]
+
+    @property
+    def local_rows(self) -> tuple[int, int]:
+        return self.rows[self.rank]
+
+    def global_chunk(self, owner: int, index: int) -> tuple[int, int]:
+        """Global row range of chunk ``index`` of rank ``owner``."""
+        start = self.rows[owner][0]
+        lo, hi = self.chunk_ranges[owner][index]
+        return start + lo, start + hi
+
+    def receivers(self) -> list[int]:
+        if self.gather == "all":
+            return [r for r in range(self.world) if r != self.rank]
+        return [0] if self.rank != 0 else []
+
+    def senders(self) -> list[int]:
+        if self.gather == "all":
+            return [r for r in range(self.world) if r != self.rank]
+        return [r for r in range(1, self.world)] if self.rank == 0 else []
+
+
+def exchange_chunk(plan: ShardPlan, index: int, c_full: torch.Tensor, group=None):
+    """Post the grouped sends/receives of chunk ``index``; returns the works (or [])."""
+    ops = []
+    lo, hi = plan.global_chunk(plan.rank, index)
+    mine = c_full[lo:hi]
+    for peer in plan.receivers():
+        ops.append(dist.P2POp(dist.isend, mine, peer, group=group))
+    for peer in plan.senders():
+        plo, phi = plan.global_chunk(peer, index)
+        ops.append(dist.P2POp(dist.irecv, c_full[plo:phi], peer, group=group))
+    if not ops:
+        return []
+    return dist.batch_isend_irecv(ops)
+
+
+def sharded_step(plan: ShardPlan, a_local: torch.Tensor, b: torch.Tensor, c_full: torch.Tensor,
+                 gemm: Callable[[torch.Tensor, torch.Tensor, torch.Tensor], None], group=None,
+                 broadcast_b: bool = True) -> None:
+    """One row-sharded GEMM: broadcast B, then per chunk GEMM + exchange.
+
+    ``gemm(a_rows, b, c_rows)`` writes ``c_rows = a_rows @ b`` on the current
+    stream.  ``c_full`` is the full M x N output (on rank 0 only needed for
+    gather="root"; other ranks may pass their full buffer or just their rows
+    as long as ``c_full[global rows]`` addresses them).
+    """
+    if broadcast_b and plan.world > 1:
+        dist.broadcast(b, src=0, group=group)
+    start, _ = plan.local_rows
+    works = []
+    for index, (lo, hi) in enumerate(plan.chunk_ranges[plan.rank]):
+        gemm(a_local[lo:hi], b, c_full[start + lo:start + hi])
+        if plan.world > 1:
+            works.extend(exchange_chunk(plan, index, c_full, group))
+    for work in works:
+        work.wait()
+
