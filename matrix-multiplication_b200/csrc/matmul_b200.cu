@@ -117,7 +117,16 @@ void launch_pack(const void *src, void *dst, int64_t rows, int64_t cols, int64_t
                                                          cols, ld);
 }
 
-// Prepare one operand for TMA: returns the pointer and leading dimension to use.
+// TF32 B: dst (n x ld) = rounded transpose of src (k x n).
+void transpose_round_b(const void *src, void *dst, int64_t k, int64_t n, int64_t ld, cudaStream_t stream)
+{
+    const int64_t nt = (n + 31) / 32, kt = (ld + 31) / 32;
+    const dim3 grid(static_cast<unsigned int>(nt < 4096 ? nt : 4096), static_cast<unsigned int>(kt < 4096 ? kt : 4096));
+    transpose_round_tf32_kernel<<<grid, dim3(32, 8), 0, stream>>>(static_cast<const float *>(src),
+                                                                  static_cast<float *>(dst), k, n, ld);
+}
+
+// Prepare one operand for TMA (copy with padding and/or TF32 rounding into scratch).
 void prepare_operand(int prec, const void *src, int64_t rows, int64_t cols, bool direct, void *scratch,
                      int64_t ld, const Context *ctx, cudaStream_t stream)
 {
@@ -158,10 +167,12 @@ int launch_tcgen05(Context *ctx, int prec, const void *a, const void *b, float *
     // TMA needs 16-byte aligned bases and row pitches; TF32 always needs rounding.
     const bool a_direct = prec != kPrecTf32 && aligned16(a) && (static_cast<int64_t>(k) * elem) % 16 == 0;
     const bool b_direct = prec != kPrecTf32 && aligned16(b) && (static_cast<int64_t>(n) * elem) % 16 == 0;
+    const bool b_transposed = prec == kPrecTf32;   // TF32 B goes K-major (n x ldb)
     const int64_t lda = a_direct ? k : round_up(k, align_elems);
-    const int64_t ldb = b_direct ? n : round_up(n, align_elems);
+    const int64_t ldb = b_direct ? n : b_transposed ? round_up(k, align_elems) : round_up(n, align_elems);
+    const int64_t b_rows = b_transposed ? n : k;
     const size_t a_bytes = a_direct ? 0 : static_cast<size_t>(round_up(static_cast<int64_t>(m) * lda * elem, 256));
-    const size_t b_bytes = b_direct ? 0 : static_cast<size_t>(round_up(static_cast<int64_t>(k) * ldb * elem, 256));
+    const size_t b_bytes = b_direct ? 0 : static_cast<size_t>(round_up(b_rows * ldb * elem, 256));
 
     void *scratch = nullptr;
     if (a_bytes + b_bytes) {
@@ -172,7 +183,10 @@ int launch_tcgen05(Context *ctx, int prec, const void *a, const void *b, float *
     const void *a_op = a_direct ? a : scratch;
     const void *b_op = b_direct ? b : static_cast<uint8_t *>(scratch) + a_bytes;
     prepare_operand(prec, a, m, k, a_direct, const_cast<void *>(a_op), lda, ctx, stream);
-    prepare_operand(prec, b, k, n, b_direct, const_cast<void *>(b_op), ldb, ctx, stream);
+    if (b_transposed)
+        transpose_round_b(b, const_cast<void *>(b_op), k, n, ldb, stream);
+    else
+        prepare_operand(prec, b, k, n, b_direct, const_cast<void *>(b_op), ldb, ctx, stream);
 
     const CUtensorMapDataType type = prec == kPrecTf32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                      : prec == kPrecBf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
@@ -182,8 +196,12 @@ int launch_tcgen05(Context *ctx, int prec, const void *a, const void *b, float *
     std::memset(&map_c, 0, sizeof(map_c));
     bool ok = encode_2d(ctx, &map_a, type, a_op, static_cast<uint64_t>(k), static_cast<uint64_t>(m),
                         static_cast<uint64_t>(lda) * elem, bk, TC_BM);
-    ok = ok && encode_2d(ctx, &map_b, type, b_op, static_cast<uint64_t>(n), static_cast<uint64_t>(k),
-                         static_cast<uint64_t>(ldb) * elem, TC_ROW_BYTES / elem, bk);
+    if (b_transposed)
+        ok = ok && encode_2d(ctx, &map_b, type, b_op, static_cast<uint64_t>(k), static_cast<uint64_t>(n),
+                             static_cast<uint64_t>(ldb) * elem, bk, TC_BN);
+    else
+        ok = ok && encode_2d(ctx, &map_b, type, b_op, static_cast<uint64_t>(n), static_cast<uint64_t>(k),
+                             static_cast<uint64_t>(ldb) * elem, TC_ROW_BYTES / elem, bk);
     const bool c_direct = !(aligned16(c) && n % 4 == 0);
     if (ok && !c_direct)
         ok = encode_2d(ctx, &map_c, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, c, static_cast<uint64_t>(n),
@@ -310,10 +328,11 @@ extern "C" int matmul_kernel_info(int implementation, int precision, char *json,
             "\"accumulator\":\"tmem_fp32\",\"tmem_columns\":%u,\"accumulator_buffers\":2,"
             "\"warp_roles\":{\"tma\":1,\"mma\":1,\"epilogue\":4},\"schedule\":\"persistent\","
             "\"raster_group_m\":%d,\"epilogue\":\"tmem_ld_smem_tma_store\","
-            "\"input_rounding\":\"%s\"}",
+            "\"input_rounding\":\"%s\",\"b_operand\":\"%s\"}",
             kPrecisionNames[precision], TC_BM, TC_BN, TC_ROW_BYTES / elem, TC_THREADS, TC_BM, TC_BN, TC_BM,
             TC_BN, TC_STAGES, precision == kPrecTf32 ? "tf32" : "f16", TC_BM, TC_BN, 32 / elem,
-            TC_TMEM_COLUMNS, kRasterGroupM, precision == kPrecTf32 ? "rne_prepass" : "none");
+            TC_TMEM_COLUMNS, kRasterGroupM, precision == kPrecTf32 ? "rne_prepass" : "none",
+            precision == kPrecTf32 ? "k_major_rounded_transpose" : "mn_major_tma");
     } else {
         written = std::snprintf(
             json, json_size,

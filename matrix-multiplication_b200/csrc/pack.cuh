@@ -68,6 +68,36 @@ __global__ void round_tf32_vec_kernel(const float4 *__restrict__ src, float4 *__
     }
 }
 
+// dst (n x ld_dst, K-major) = TF32-rounded transpose of src (k x n, row-major),
+// zero in the padding columns k .. ld_dst-1.  32 x 32 tiles through shared
+// memory so that both the global reads (along n) and writes (along k) coalesce.
+// The tensor core reads MN-major TF32 operands only in a 32-byte-atom swizzle,
+// so the TF32 path hands it a K-major B produced here, in the same pass that
+// rounds the values.
+__global__ void transpose_round_tf32_kernel(const float *__restrict__ src, float *__restrict__ dst, int64_t k,
+                                            int64_t n, int64_t ld_dst)
+{
+    __shared__ float tile[32][33];
+    const int64_t n_tiles = (n + 31) / 32;
+    const int64_t k_tiles = (ld_dst + 31) / 32;
+    for (int64_t kt = blockIdx.y; kt < k_tiles; kt += gridDim.y) {
+        for (int64_t nt = blockIdx.x; nt < n_tiles; nt += gridDim.x) {
+            const int64_t n0 = nt * 32, k0 = kt * 32;
+            for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+                const int64_t kk = k0 + r, nn = n0 + threadIdx.x;
+                tile[r][threadIdx.x] = (kk < k && nn < n) ? round_tf32_rne(src[kk * n + nn]) : 0.0f;
+            }
+            __syncthreads();
+            for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+                const int64_t nn = n0 + r, kk = k0 + threadIdx.x;
+                if (nn < n && kk < ld_dst)
+                    dst[nn * ld_dst + kk] = tile[threadIdx.x][r];
+            }
+            __syncthreads();
+        }
+    }
+}
+
 template <typename T>
 __device__ __forceinline__ T convert_one(float x);
 template <>

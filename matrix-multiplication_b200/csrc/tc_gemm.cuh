@@ -17,11 +17,13 @@
 //               is not TMA-compatible, store directly with bounds checks).
 //               Runs one tile behind the MMA thanks to the two accumulators.
 //
-// A is K-major in shared memory; B stays row-major (N contiguous), i.e. the
-// MN-major operand form of the instruction descriptor, so neither operand is
-// transposed in memory.  Tiles are visited persistently (tile += gridDim.x)
-// in groups of `group_m` M-blocks so that concurrently running CTAs share A
-// and B panels in L2.
+// A is K-major in shared memory.  For FP16/BF16, B stays row-major (N
+// contiguous), i.e. the MN-major operand form of the instruction descriptor,
+// so neither operand is transposed in memory.  TF32 operands are rounded by a
+// pre-pass anyway, and that pass also transposes B so that TF32 B is K-major
+// like A (MN-major TF32 would need the 32-byte-atom swizzle).  Tiles are
+// visited persistently (tile += gridDim.x) in groups of `group_m` M-blocks so
+// that concurrently running CTAs share A and B panels in L2.
 #pragma once
 
 #include <cuda.h>
@@ -72,12 +74,12 @@ struct TcParams {
 };
 
 // Instruction descriptor (kind::f16 / kind::tf32): FP32 accumulator (bits 4-5 = 1),
-// A/B formats (bits 7-9, 10-12), A K-major (bit 15 = 0), B MN-major (bit 16 = 1),
-// N >> 3 in bits 17-22, M >> 4 in bits 24-28.
-__host__ __device__ constexpr uint32_t tc_instr_desc(int fmt)
+// A/B formats (bits 7-9, 10-12), A K-major (bit 15 = 0), B MN-major (bit 16 = 1)
+// or K-major (0), N >> 3 in bits 17-22, M >> 4 in bits 24-28.
+__host__ __device__ constexpr uint32_t tc_instr_desc(int fmt, bool b_k_major)
 {
     return (1u << 4) | (static_cast<uint32_t>(fmt) << 7) | (static_cast<uint32_t>(fmt) << 10) |
-           (0u << 15) | (1u << 16) | (static_cast<uint32_t>(TC_BN >> 3) << 17) |
+           (0u << 15) | ((b_k_major ? 0u : 1u) << 16) | (static_cast<uint32_t>(TC_BN >> 3) << 17) |
            (static_cast<uint32_t>(TC_BM >> 4) << 24);
 }
 
@@ -105,7 +107,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     constexpr int kNB = TC_ROW_BYTES / kElem;          // B box width in elements (64 or 32)
     constexpr int kBBoxes = TC_BN / kNB;               // 4 or 8
     constexpr uint32_t kBBoxBytes = kBK * TC_ROW_BYTES;  // bytes per B column block
-    constexpr uint32_t kIdesc = tc_instr_desc(FMT);
+    constexpr bool kBKMajor = kTF32;                     // TF32 B arrives transposed
+    constexpr uint32_t kIdesc = tc_instr_desc(FMT, kBKMajor);
 
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_addr(smem_raw);
@@ -170,10 +173,15 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                     }
                     mbar_arrive_expect_tx(full_bar(stage), TC_A_STAGE + TC_B_STAGE);
                     tma_load_2d(s_a + stage * TC_A_STAGE, &map_a, full_bar(stage), kb * kBK, mb * TC_BM);
+                    if constexpr (kBKMajor) {
+                        // B^T tile: TC_BN rows (n) x 128 bytes (k), one box.
+                        tma_load_2d(s_b + stage * TC_B_STAGE, &map_b, full_bar(stage), kb * kBK, nb * TC_BN);
+                    } else {
 #pragma unroll
-                    for (int j = 0; j < kBBoxes; ++j)
-                        tma_load_2d(s_b + stage * TC_B_STAGE + j * kBBoxBytes, &map_b, full_bar(stage),
-                                    nb * TC_BN + j * kNB, kb * kBK);
+                        for (int j = 0; j < kBBoxes; ++j)
+                            tma_load_2d(s_b + stage * TC_B_STAGE + j * kBBoxBytes, &map_b, full_bar(stage),
+                                        nb * TC_BN + j * kNB, kb * kBK);
+                    }
                     filled |= 1u << stage;
                     fill_parity = (fill_parity & ~(1u << stage)) | (phase << stage);
                     if (++stage == TC_STAGES) {
@@ -217,10 +225,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                     for (int kk = 0; kk < kMmasPerStage; ++kk) {
                         // A: K-major SW128, K slice kk starts 32 bytes further inside each row.
                         const uint64_t a_desc = smem_desc_sw128(a_stage + kk * 32, 16, 1024);
-                        // B: MN-major SW128, K slice kk starts kMmaK rows (x 128 B) further;
-                        // column blocks are kBBoxBytes apart.
+                        // B: K-major like A, or MN-major SW128 where K slice kk starts kMmaK
+                        // rows (x 128 B) further and column blocks are kBBoxBytes apart.
                         const uint64_t b_desc =
-                            smem_desc_sw128(b_stage + kk * kMmaK * TC_ROW_BYTES, kBBoxBytes, 1024);
+                            kBKMajor ? smem_desc_sw128(b_stage + kk * 32, 16, 1024)
+                                     : smem_desc_sw128(b_stage + kk * kMmaK * TC_ROW_BYTES, kBBoxBytes, 1024);
                         tc_mma<kTF32>(d_tmem, a_desc, b_desc, kIdesc, (kb | kk) != 0 ? 1u : 0u);
                     }
                     tc_commit(empty_bar(stage));

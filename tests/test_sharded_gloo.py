@@ -1,0 +1,100 @@
+"""Host logic of the row-sharded multi-GPU GEMM on CPU ranks (gloo, world size 2
+and 3): row plans, the B broadcast and the chunked all-gather / gather-to-root
+exchange, with an FP32 torch product standing in for the GPU kernel."""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from sharded import ShardPlan, chunk_rows, shard_rows, sharded_step
+
+
+def test_shard_rows_partition_every_row_once():
+    for m in (1, 7, 8, 37, 32768):
+        for world in (1, 2, 3, 8):
+            ranges = [shard_rows(m, world, r) for r in range(world)]
+            assert ranges[0][0] == 0 and ranges[-1][1] == m
+            for (s0, e0), (s1, e1) in zip(ranges, ranges[1:]):
+                assert e0 == s1
+            sizes = [e - s for s, e in ranges]
+            assert max(sizes) - min(sizes) <= 1
+    with pytest.raises(ValueError):
+        shard_rows(8, 2, 2)
+
+
+def test_chunk_rows():
+    assert chunk_rows(10, 3) == [(0, 4), (4, 7), (7, 10)]
+    assert chunk_rows(2, 4) == [(0, 1), (1, 2)]
+    assert chunk_rows(0, 4) == []
+
+
+def test_plan_peers():
+    plan = ShardPlan(64, 8, 8, 4, 2, chunks=2, gather="all")
+    assert plan.receivers() == [0, 1, 3] and plan.senders() == [0, 1, 3]
+    root = ShardPlan(64, 8, 8, 4, 0, chunks=2, gather="root")
+    assert root.receivers() == [] and root.senders() == [1, 2, 3]
+    leaf = ShardPlan(64, 8, 8, 4, 3, chunks=2, gather="root")
+    assert leaf.receivers() == [0] and leaf.senders() == []
+    assert plan.global_chunk(1, 1) == (24, 32)
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _cpu_gemm(a_rows, b, c_rows):
+    torch.matmul(a_rows, b, out=c_rows)
+
+
+def _worker(rank, world, port, m, k, n, chunks, gather, results):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        torch.manual_seed(0)
+        a_full = torch.randn(m, k)
+        b_full = torch.randn(k, n)
+        plan = ShardPlan(m, k, n, world, rank, chunks=chunks, gather=gather)
+        start, stop = plan.local_rows
+        a_local = a_full[start:stop].clone()
+        b = b_full.clone() if rank == 0 else torch.zeros(k, n)
+        c = torch.full((m, n), float("nan"))
+        for _ in range(2):
+            sharded_step(plan, a_local, b, c, _cpu_gemm)
+        expected = a_full @ b_full
+        if gather == "all" or rank == 0:
+            ok = torch.allclose(c, expected, rtol=1e-5, atol=1e-4)
+        else:
+            ok = torch.allclose(c[start:stop], expected[start:stop], rtol=1e-5, atol=1e-4)
+        ok = ok and torch.equal(b, b_full)
+        results[rank] = bool(ok)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,m,chunks,gather", [(2, 64, 4, "all"), (2, 37, 3, "all"), (3, 50, 2, "root"),
+                                                    (2, 5, 8, "root")])
+def test_row_sharded_gemm_on_gloo_ranks(world, m, chunks, gather):
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    results = manager.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, m, 24, 40, chunks, gather, results))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert all(p.exitcode == 0 for p in procs)
+    assert dict(results) == {r: True for r in range(world)}
