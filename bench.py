@@ -430,7 +430,8 @@ def multi_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
 def main() -> int:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--gpus", type=int, default=1)
-    parser.add_argument("--steps", type=int, default=200)
+    parser.add_argument("--steps", type=int, default=None,
+                        help="timed steps (default 500 for square8192, 20 for rowshard32768)")
     parser.add_argument("--warmup", type=int, default=10)
     parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
     parser.add_argument("--workload", choices=("square8192", "rowshard32768"), default=None)
@@ -446,6 +447,8 @@ def main() -> int:
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.workload is None:
         args.workload = "square8192" if args.gpus == 1 else "rowshard32768"
+    if args.steps is None:
+        args.steps = 500 if args.workload == "square8192" else 20
     if args.impl == "reference":
         run_reference_arm(args, rank)
         return 0
