@@ -17,6 +17,7 @@
 #include "ffma_gemm.cuh"
 #include "pack.cuh"
 #include "tc_gemm.cuh"
+#include "tc2_gemm.cuh"
 
 namespace {
 
@@ -27,6 +28,7 @@ constexpr int kImplTcgen05 = 7;
 constexpr int kImplFfma = 8;
 constexpr int kPrecFp32 = 0, kPrecTf32 = 1, kPrecFp16 = 2, kPrecBf16 = 3;
 constexpr int kRasterGroupM = 16;
+constexpr int kRasterGroupMPair = 8;
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                    const cuuint64_t *, const cuuint32_t *, const cuuint32_t *,
@@ -38,6 +40,7 @@ struct Context {
     int major = 0;
     int minor = 0;
     int sm_count = 0;
+    int max_pairs = 0;        // co-resident 2-CTA clusters of the pair kernel
     EncodeTiledFn encode = nullptr;
     cudaMemPool_t pool = nullptr;
 };
@@ -152,10 +155,13 @@ void prepare_operand(int prec, const void *src, int64_t rows, int64_t cols, bool
 }
 
 template <int FMT>
-cudaError_t launch_tc_kernel(const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &mc,
+cudaError_t launch_tc_kernel(bool pair, const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &mc,
                              const TcParams &params, int grid, cudaStream_t stream)
 {
-    tc_gemm_kernel<FMT><<<grid, TC_THREADS, TC_SMEM_BYTES, stream>>>(ma, mb, mc, params);
+    if (pair)
+        tc2_gemm_kernel<FMT><<<grid, TC_THREADS, TC2_SMEM_BYTES, stream>>>(ma, mb, mc, params);
+    else
+        tc_gemm_kernel<FMT><<<grid, TC_THREADS, TC_SMEM_BYTES, stream>>>(ma, mb, mc, params);
     return cudaGetLastError();
 }
 
@@ -188,6 +194,10 @@ int launch_tcgen05(Context *ctx, int prec, const void *a, const void *b, float *
     else
         prepare_operand(prec, b, k, n, b_direct, const_cast<void *>(b_op), ldb, ctx, stream);
 
+    // CTA pairs (256 x 256 tiles) whenever there is more than one 128-row block.
+    const bool pair = m > TC_BM && ctx->max_pairs > 0;
+    const int tile_m = pair ? TC2_BM : TC_BM;
+    const int tile_n = pair ? TC2_BN : TC_BN;
     const CUtensorMapDataType type = prec == kPrecTf32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                      : prec == kPrecBf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                          : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -198,7 +208,7 @@ int launch_tcgen05(Context *ctx, int prec, const void *a, const void *b, float *
                         static_cast<uint64_t>(lda) * elem, bk, TC_BM);
     if (b_transposed)
         ok = ok && encode_2d(ctx, &map_b, type, b_op, static_cast<uint64_t>(k), static_cast<uint64_t>(n),
-                             static_cast<uint64_t>(ldb) * elem, bk, TC_BN);
+                             static_cast<uint64_t>(ldb) * elem, bk, pair ? TC2_HALF : TC_BN);
     else
         ok = ok && encode_2d(ctx, &map_b, type, b_op, static_cast<uint64_t>(n), static_cast<uint64_t>(k),
                              static_cast<uint64_t>(ldb) * elem, TC_ROW_BYTES / elem, bk);
@@ -217,8 +227,8 @@ int launch_tcgen05(Context *ctx, int prec, const void *a, const void *b, float *
     params.m = m;
     params.n = n;
     params.k = k;
-    params.num_m_blocks = (m + TC_BM - 1) / TC_BM;
-    params.num_n_blocks = (n + TC_BN - 1) / TC_BN;
+    params.num_m_blocks = (m + tile_m - 1) / tile_m;
+    params.num_n_blocks = (n + tile_n - 1) / tile_n;
     params.num_k_blocks = static_cast<int>((static_cast<int64_t>(k) + bk - 1) / bk);
     const int64_t tiles = static_cast<int64_t>(params.num_m_blocks) * params.num_n_blocks;
     if (tiles > 0x7fffffff) {
@@ -227,18 +237,21 @@ int launch_tcgen05(Context *ctx, int prec, const void *a, const void *b, float *
         return fail(error, error_size, "matmul_launch", "too many output tiles");
     }
     params.num_tiles = static_cast<int>(tiles);
-    params.group_m = kRasterGroupM;
+    // 8 pair blocks (2048 rows) or 16 single blocks per raster group: about as
+    // many A row blocks as B column blocks in flight across the 148 SMs.
+    params.group_m = pair ? kRasterGroupMPair : kRasterGroupM;
     params.c = c;
     params.c_direct = c_direct ? 1 : 0;
-    const int grid = static_cast<int>(tiles < ctx->sm_count ? tiles : ctx->sm_count);
+    const int units = pair ? ctx->max_pairs : ctx->sm_count;
+    const int grid = static_cast<int>(tiles < units ? tiles : units) * (pair ? 2 : 1);
 
     cudaError_t st;
     if (prec == kPrecTf32)
-        st = launch_tc_kernel<kFmtTF32>(map_a, map_b, map_c, params, grid, stream);
+        st = launch_tc_kernel<kFmtTF32>(pair, map_a, map_b, map_c, params, grid, stream);
     else if (prec == kPrecBf16)
-        st = launch_tc_kernel<kFmtBF16>(map_a, map_b, map_c, params, grid, stream);
+        st = launch_tc_kernel<kFmtBF16>(pair, map_a, map_b, map_c, params, grid, stream);
     else
-        st = launch_tc_kernel<kFmtF16>(map_a, map_b, map_c, params, grid, stream);
+        st = launch_tc_kernel<kFmtF16>(pair, map_a, map_b, map_c, params, grid, stream);
     if (scratch)
         cudaFreeAsync(scratch, stream);
     if (st != cudaSuccess)
@@ -324,15 +337,17 @@ extern "C" int matmul_kernel_info(int implementation, int precision, char *json,
             "{\"implementation\":\"tcgen05\",\"precision\":\"%s\",\"tile_m\":%d,\"tile_n\":%d,"
             "\"tile_k\":%d,\"threads\":%d,\"warp_tile_m\":%d,\"warp_tile_n\":%d,\"microtile_m\":%d,"
             "\"microtile_n\":%d,\"buffering\":%d,\"load_method\":\"tma_sw128\",\"tensor_cores\":true,"
-            "\"mma\":\"tcgen05.mma.cta_group::1.kind::%s\",\"mma_shape\":[%d,%d,%d],"
+            "\"mma\":\"tcgen05.mma.cta_group::2.kind::%s\",\"mma_shape\":[%d,%d,%d],\"cluster\":[2,1,1],"
             "\"accumulator\":\"tmem_fp32\",\"tmem_columns\":%u,\"accumulator_buffers\":2,"
             "\"warp_roles\":{\"tma\":1,\"mma\":1,\"epilogue\":4},\"schedule\":\"persistent\","
-            "\"raster_group_m\":%d,\"epilogue\":\"tmem_ld_smem_tma_store\","
-            "\"input_rounding\":\"%s\",\"b_operand\":\"%s\"}",
-            kPrecisionNames[precision], TC_BM, TC_BN, TC_ROW_BYTES / elem, TC_THREADS, TC_BM, TC_BN, TC_BM,
-            TC_BN, TC_STAGES, precision == kPrecTf32 ? "tf32" : "f16", TC_BM, TC_BN, 32 / elem,
-            TC_TMEM_COLUMNS, kRasterGroupM, precision == kPrecTf32 ? "rne_prepass" : "none",
-            precision == kPrecTf32 ? "k_major_rounded_transpose" : "mn_major_tma");
+            "\"raster_group_m\":%d,\"epilogue\":\"tmem_ld_smem_tma_store\",\"input_rounding\":\"%s\","
+            "\"b_operand\":\"%s\",\"small_m_kernel\":{\"max_m\":%d,\"cta_group\":1,\"tile_m\":%d,"
+            "\"tile_n\":%d,\"buffering\":%d,\"raster_group_m\":%d}}",
+            kPrecisionNames[precision], TC2_BM, TC2_BN, TC_ROW_BYTES / elem, TC_THREADS, TC2_HALF, TC2_BN, TC2_HALF,
+            TC2_BN, TC2_STAGES, precision == kPrecTf32 ? "tf32" : "f16", TC2_BM, TC2_BN, 32 / elem,
+            TC_TMEM_COLUMNS, kRasterGroupMPair, precision == kPrecTf32 ? "rne_prepass" : "none",
+            precision == kPrecTf32 ? "k_major_rounded_transpose" : "mn_major_tma", TC_BM, TC_BM, TC_BN, TC_STAGES,
+            kRasterGroupM);
     } else {
         written = std::snprintf(
             json, json_size,
@@ -409,6 +424,38 @@ extern "C" void *matmul_create(int device, char *error, size_t error_size)
             fail_cuda(error, error_size, "cudaFuncSetAttribute", st);
             return nullptr;
         }
+    }
+    const void *tc2_kernels[] = {reinterpret_cast<const void *>(&tc2_gemm_kernel<kFmtF16>),
+                                 reinterpret_cast<const void *>(&tc2_gemm_kernel<kFmtBF16>),
+                                 reinterpret_cast<const void *>(&tc2_gemm_kernel<kFmtTF32>)};
+    for (const void *kernel : tc2_kernels) {
+        st = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TC2_SMEM_BYTES);
+        if (st != cudaSuccess) {
+            delete ctx;
+            fail_cuda(error, error_size, "cudaFuncSetAttribute", st);
+            return nullptr;
+        }
+    }
+    // How many 2-CTA clusters of the pair kernel fit on the device at once.
+    {
+        cudaLaunchConfig_t config{};
+        config.gridDim = dim3(2 * (sms / 2), 1, 1);
+        config.blockDim = dim3(TC_THREADS, 1, 1);
+        config.dynamicSmemBytes = TC2_SMEM_BYTES;
+        cudaLaunchAttribute attribute{};
+        attribute.id = cudaLaunchAttributeClusterDimension;
+        attribute.val.clusterDim.x = 2;
+        attribute.val.clusterDim.y = 1;
+        attribute.val.clusterDim.z = 1;
+        config.attrs = &attribute;
+        config.numAttrs = 1;
+        int clusters = 0;
+        st = cudaOccupancyMaxActiveClusters(&clusters, tc2_kernels[1], &config);
+        if (st != cudaSuccess) {
+            cudaGetLastError();
+            clusters = 0;
+        }
+        ctx->max_pairs = clusters;
     }
 
     cudaMemPoolProps props{};

@@ -76,11 +76,11 @@ struct TcParams {
 // Instruction descriptor (kind::f16 / kind::tf32): FP32 accumulator (bits 4-5 = 1),
 // A/B formats (bits 7-9, 10-12), A K-major (bit 15 = 0), B MN-major (bit 16 = 1)
 // or K-major (0), N >> 3 in bits 17-22, M >> 4 in bits 24-28.
-__host__ __device__ constexpr uint32_t tc_instr_desc(int fmt, bool b_k_major)
+__host__ __device__ constexpr uint32_t tc_instr_desc(int fmt, bool b_k_major, int mma_m = TC_BM, int mma_n = TC_BN)
 {
     return (1u << 4) | (static_cast<uint32_t>(fmt) << 7) | (static_cast<uint32_t>(fmt) << 10) |
-           (0u << 15) | ((b_k_major ? 0u : 1u) << 16) | (static_cast<uint32_t>(TC_BN >> 3) << 17) |
-           (static_cast<uint32_t>(TC_BM >> 4) << 24);
+           (0u << 15) | ((b_k_major ? 0u : 1u) << 16) | (static_cast<uint32_t>(mma_n >> 3) << 17) |
+           (static_cast<uint32_t>(mma_m >> 4) << 24);
 }
 
 __device__ __forceinline__ void tc_tile_coords(int tile, const TcParams &p, int &mb, int &nb)
@@ -202,6 +202,14 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         if (lane == 0) {
             int stage = 0;
             uint32_t phase = 0;
+            // Loop-invariant descriptor halves: only the start-address field (bits 0-13,
+            // address >> 4) moves between stages and K slices, so the issue loop adds.
+            const uint64_t a_desc0 = smem_desc_sw128(s_a, 16, 1024);
+            const uint64_t b_desc0 = kBKMajor ? smem_desc_sw128(s_b, 16, 1024) : smem_desc_sw128(s_b, kBBoxBytes, 1024);
+            constexpr uint64_t kADescStage = TC_A_STAGE >> 4;
+            constexpr uint64_t kBDescStage = TC_B_STAGE >> 4;
+            constexpr uint64_t kADescK = 32 >> 4;
+            constexpr uint64_t kBDescK = kBKMajor ? (32 >> 4) : ((kMmaK * TC_ROW_BYTES) >> 4);
             int acc = 0;
             uint32_t acc_phase = 0;
             bool ok = true;
@@ -219,19 +227,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a_stage = s_a + stage * TC_A_STAGE;
-                    const uint32_t b_stage = s_b + stage * TC_B_STAGE;
+                    const uint64_t a_desc = a_desc0 + static_cast<uint64_t>(stage) * kADescStage;
+                    const uint64_t b_desc = b_desc0 + static_cast<uint64_t>(stage) * kBDescStage;
 #pragma unroll
-                    for (int kk = 0; kk < kMmasPerStage; ++kk) {
-                        // A: K-major SW128, K slice kk starts 32 bytes further inside each row.
-                        const uint64_t a_desc = smem_desc_sw128(a_stage + kk * 32, 16, 1024);
-                        // B: K-major like A, or MN-major SW128 where K slice kk starts kMmaK
-                        // rows (x 128 B) further and column blocks are kBBoxBytes apart.
-                        const uint64_t b_desc =
-                            kBKMajor ? smem_desc_sw128(b_stage + kk * 32, 16, 1024)
-                                     : smem_desc_sw128(b_stage + kk * kMmaK * TC_ROW_BYTES, kBBoxBytes, 1024);
-                        tc_mma<kTF32>(d_tmem, a_desc, b_desc, kIdesc, (kb | kk) != 0 ? 1u : 0u);
-                    }
+                    for (int kk = 0; kk < kMmasPerStage; ++kk)
+                        tc_mma<kTF32>(d_tmem, a_desc + kk * kADescK, b_desc + kk * kBDescK, kIdesc,
+                                      (kb | kk) != 0 ? 1u : 0u);
                     tc_commit(empty_bar(stage));
                     if (++stage == TC_STAGES) {
                         stage = 0;
