@@ -75,6 +75,26 @@ int matmul_convert(void *context, int precision, const float *src, void *dst, si
 int matmul_device_status(void *context, int clear, unsigned int *status,
                          char *error, size_t error_size);
 
+/* No counterpart in the reference.  Same arguments, result and error convention
+ * as matmul_launch, for implementation 7 (tcgen05) only, but it never allocates:
+ * for callers that must not call cudaMalloc or a stream-ordered allocator --
+ * a process whose framework has already reserved nearly all device memory in
+ * its own pool, or code that captures a graph in which it may add no memory
+ * nodes.  The TF32 rounding copies and the repacked copies of unaligned operands
+ * that matmul_launch places in pool memory go instead into one fixed 32 MiB
+ * array compiled into the library (every GPU that loads the library holds it
+ * until the process exits).  A problem whose copies need more than 32 MiB is
+ * rejected with "matmul_launch_noalloc: this problem needs N bytes of scratch,
+ * more than the fixed ..." (TF32 needs 4*(m*k' + n*k') bytes with k' = k
+ * rounded up to 4; aligned BF16/FP16 operands need none).  The first call on a
+ * device looks up the array's device address with that device current; make
+ * that first call before any stream capture.  All calls share the one array and
+ * every call rewrites the part it uses, so calls that overlap on the GPU (other
+ * streams, or other threads) race: order them on one stream. */
+int matmul_launch_noalloc(void *context, int implementation, int precision,
+                          const void *a, const void *b, float *c, int m, int k, int n,
+                          void *stream, char *error, size_t error_size);
+
 #ifdef __cplusplus
 }
 #endif

@@ -12,6 +12,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <new>
 
 #include "ffma_gemm.cuh"
@@ -19,9 +20,38 @@
 #include "tc_gemm.cuh"
 #include "tc2_gemm.cuh"
 
+// Scratch for matmul_launch_noalloc: a fixed array in the module's device
+// memory, so that entry point never allocates.  Every GPU that loads this
+// library holds these bytes until the process exits.
+constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;   // 32 MiB
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
 namespace {
 
 using namespace b200;
+
+// Device address of g_noalloc_scratch per device, looked up once per device with
+// that device current.  In host code the symbol itself is only a host-side
+// stand-in, never a device address.
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+void *g_noalloc_address[kMaxDevices] = {};
+
+cudaError_t noalloc_scratch_address(int device, void **address)
+{
+    if (device < 0 || device >= kMaxDevices)
+        return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (!g_noalloc_address[device]) {
+        void *ptr = nullptr;
+        const cudaError_t st = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+        if (st != cudaSuccess)
+            return st;
+        g_noalloc_address[device] = ptr;
+    }
+    *address = g_noalloc_address[device];
+    return cudaSuccess;
+}
 
 constexpr int kAbiVersion = 3;
 constexpr int kImplTcgen05 = 7;
@@ -166,7 +196,8 @@ cudaError_t launch_tc_kernel(bool pair, const CUtensorMap &ma, const CUtensorMap
 }
 
 int launch_tcgen05(Context *ctx, int prec, const void *a, const void *b, float *c, int m, int k, int n,
-                   cudaStream_t stream, char *error, size_t error_size)
+                   cudaStream_t stream, char *error, size_t error_size, void *fixed_scratch = nullptr,
+                   size_t fixed_scratch_bytes = 0)
 {
     const int elem = prec == kPrecTf32 ? 4 : 2;
     const int64_t align_elems = 16 / elem;
@@ -181,11 +212,23 @@ int launch_tcgen05(Context *ctx, int prec, const void *a, const void *b, float *
     const size_t b_bytes = b_direct ? 0 : static_cast<size_t>(round_up(b_rows * ldb * elem, 256));
 
     void *scratch = nullptr;
-    if (a_bytes + b_bytes) {
+    if (a_bytes + b_bytes && fixed_scratch) {
+        if (a_bytes + b_bytes > fixed_scratch_bytes) {
+            char detail[200];
+            std::snprintf(detail, sizeof(detail),
+                          "this problem needs %zu bytes of scratch, more than the fixed %zu-byte array; "
+                          "use matmul_launch",
+                          a_bytes + b_bytes, fixed_scratch_bytes);
+            return fail(error, error_size, "matmul_launch_noalloc", detail);
+        }
+        scratch = fixed_scratch;
+    } else if (a_bytes + b_bytes) {
         const cudaError_t st = scratch_alloc(ctx, &scratch, a_bytes + b_bytes, stream);
         if (st != cudaSuccess)
             return fail_cuda(error, error_size, "matmul_launch: scratch allocation", st);
     }
+    // Only scratch taken from the stream-ordered pool is handed back.
+    void *pooled = fixed_scratch ? nullptr : scratch;
     const void *a_op = a_direct ? a : scratch;
     const void *b_op = b_direct ? b : static_cast<uint8_t *>(scratch) + a_bytes;
     prepare_operand(prec, a, m, k, a_direct, const_cast<void *>(a_op), lda, ctx, stream);
@@ -217,8 +260,8 @@ int launch_tcgen05(Context *ctx, int prec, const void *a, const void *b, float *
         ok = encode_2d(ctx, &map_c, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, c, static_cast<uint64_t>(n),
                        static_cast<uint64_t>(m), static_cast<uint64_t>(n) * 4, 32, 32);
     if (!ok) {
-        if (scratch)
-            cudaFreeAsync(scratch, stream);
+        if (pooled)
+            cudaFreeAsync(pooled, stream);
         cudaGetLastError();
         return fail(error, error_size, "matmul_launch", "cuTensorMapEncodeTiled rejected an operand");
     }
@@ -232,8 +275,8 @@ int launch_tcgen05(Context *ctx, int prec, const void *a, const void *b, float *
     params.num_k_blocks = static_cast<int>((static_cast<int64_t>(k) + bk - 1) / bk);
     const int64_t tiles = static_cast<int64_t>(params.num_m_blocks) * params.num_n_blocks;
     if (tiles > 0x7fffffff) {
-        if (scratch)
-            cudaFreeAsync(scratch, stream);
+        if (pooled)
+            cudaFreeAsync(pooled, stream);
         return fail(error, error_size, "matmul_launch", "too many output tiles");
     }
     params.num_tiles = static_cast<int>(tiles);
@@ -252,8 +295,8 @@ int launch_tcgen05(Context *ctx, int prec, const void *a, const void *b, float *
         st = launch_tc_kernel<kFmtBF16>(pair, map_a, map_b, map_c, params, grid, stream);
     else
         st = launch_tc_kernel<kFmtF16>(pair, map_a, map_b, map_c, params, grid, stream);
-    if (scratch)
-        cudaFreeAsync(scratch, stream);
+    if (pooled)
+        cudaFreeAsync(pooled, stream);
     if (st != cudaSuccess)
         return fail(error, error_size, "kernel launch", cudaGetErrorString(st));
     return 0;
@@ -574,4 +617,37 @@ extern "C" int matmul_device_status(void *opaque, int clear, unsigned int *statu
     if (st != cudaSuccess)
         return fail_cuda(error, error_size, "matmul_device_status", st);
     return 0;
+}
+
+extern "C" int matmul_launch_noalloc(void *opaque, int implementation, int precision, const void *a,
+                                     const void *b, float *c, int m, int k, int n, void *stream, char *error,
+                                     size_t error_size)
+{
+    clear_error(error, error_size);
+    if (!opaque)
+        return fail(error, error_size, "matmul_launch_noalloc", "context is null");
+    if (!a || !b || !c)
+        return fail(error, error_size, "matmul_launch_noalloc", "matrix pointer is null");
+    if (m <= 0 || k <= 0 || n <= 0)
+        return fail(error, error_size, "matmul_launch_noalloc", "dimensions must be positive");
+    if (check_ids(implementation, precision, "matmul_launch_noalloc", error, error_size))
+        return 1;
+    if (implementation != kImplTcgen05)
+        return fail(error, error_size, "matmul_launch_noalloc",
+                    "only implementation 7 (tcgen05) has a fixed-scratch variant; the FFMA kernel needs no "
+                    "scratch, use matmul_launch");
+    const size_t elem = precision == kPrecFp16 || precision == kPrecBf16 ? 2 : 4;
+    if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b)) % elem ||
+        reinterpret_cast<uintptr_t>(c) % 4)
+        return fail(error, error_size, "matmul_launch_noalloc", "matrix pointer is not aligned to its element size");
+    Context *ctx = static_cast<Context *>(opaque);
+    cudaError_t st = cudaSetDevice(ctx->device);
+    if (st != cudaSuccess)
+        return fail_cuda(error, error_size, "cudaSetDevice", st);
+    void *scratch = nullptr;
+    st = noalloc_scratch_address(ctx->device, &scratch);
+    if (st != cudaSuccess)
+        return fail_cuda(error, error_size, "matmul_launch_noalloc: cudaGetSymbolAddress", st);
+    return launch_tcgen05(ctx, precision, a, b, c, m, k, n, static_cast<cudaStream_t>(stream), error, error_size,
+                          scratch, kNoAllocScratchBytes);
 }
