@@ -439,6 +439,9 @@ def main() -> int:
     parser.add_argument("--chunks", type=int, default=4)
     parser.add_argument("--gather", choices=("all", "root"), default="all")
     parser.add_argument("--quick", action="store_true", help="skip the per-precision and cuBLAS tables")
+    parser.add_argument("--sweep", choices=("square", "llm", "ragged", "all"), default=None,
+                        help="instead of the contract line, time every shape of a configuration "
+                             "(reference graph method, one JSON line per case, torch/cuBLAS beside it)")
     args = parser.parse_args()
     if args.warmup < 3:
         parser.error("at least 3 warm-up steps")
@@ -449,6 +452,9 @@ def main() -> int:
         args.workload = "square8192" if args.gpus == 1 else "rowshard32768"
     if args.steps is None:
         args.steps = 500 if args.workload == "square8192" else 20
+    if args.sweep:
+        sweep(args.sweep)
+        return 0
     if args.impl == "reference":
         run_reference_arm(args, rank)
         return 0
@@ -463,6 +469,77 @@ def main() -> int:
     if line is not None:
         print(json.dumps(line), flush=True)
     return 0
+
+
+SWEEPS = {
+    # square size sweep 64..4096 at every precision, U[-1,1)
+    "square": [(s, s, s, p, "uniform") for s in (64, 128, 256, 512, 1024, 2048, 4096)
+               for p in ("fp32", "tf32", "fp16", "bf16")],
+    # large and LLM-like shapes, BF16 and FP16, N(0, 1/sqrt(K))
+    "llm": [(m, k, n, p, "normal") for (m, k, n) in ((8192, 8192, 8192), (16, 8192, 8192),
+                                                      (8192, 8192, 28672), (4096, 14336, 4096))
+            for p in ("bf16", "fp16")],
+    # ragged partial-tile shapes, FP32 and BF16
+    "ragged": [(m, k, n, p, "uniform") for (m, k, n) in ((31, 33, 65), (511, 257, 129), (513, 129, 577))
+               for p in ("fp32", "bf16")],
+}
+
+
+def sweep(which: str) -> None:
+    """Time each case with the reference's CUDA-graph method; print one JSON line per case."""
+    import torch
+
+    from gpumat import NativeMatmul
+    from precision import INPUT_DTYPES, torch_precision
+
+    peaks, _ = load_peaks()
+    cases = [c for key in (("square", "llm", "ragged") if which == "all" else (which,)) for c in SWEEPS[key]]
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    native = NativeMatmul(device=0)
+    stream = torch.cuda.Stream(device=device)
+    for m, k, n, precision, dist in cases:
+        backend = "ffma" if precision == "fp32" else "tcgen05"
+        dtype = getattr(torch, INPUT_DTYPES[precision])
+        gen = torch.Generator(device=device)
+        gen.manual_seed(m * 7 + k * 3 + n)
+        with torch.cuda.stream(stream):
+            if dist == "normal":
+                a32 = torch.randn((m, k), generator=gen, device=device) * (k ** -0.5)
+                b32 = torch.randn((k, n), generator=gen, device=device) * (k ** -0.5)
+            else:
+                a32 = torch.rand((m, k), generator=gen, device=device) * 2 - 1
+                b32 = torch.rand((k, n), generator=gen, device=device) * 2 - 1
+            a = torch.empty((m, k), dtype=dtype, device=device)
+            b = torch.empty((k, n), dtype=dtype, device=device)
+            native.convert(a32, a, precision)
+            native.convert(b32, b, precision)
+            del a32, b32
+            c = torch.empty((m, n), dtype=torch.float32, device=device)
+            ref = torch.empty((m, n), dtype=torch.float32, device=device)
+            run = native.prepare(backend, a, b, c, precision=precision)
+        ours = reference_method(run, stream, m, k, n)
+        with torch_precision(torch, precision):
+            if precision in ("fp16", "bf16"):
+                trun = lambda: torch.mm(a, b, out_dtype=torch.float32, out=ref)
+            else:
+                trun = lambda: torch.mm(a, b, out=ref)
+            theirs = reference_method(trun, stream, m, k, n)
+        stream.synchronize()
+        diff = float((c - ref).abs().max().item())
+        bytes_min = (4 if precision in ("fp32", "tf32") else 2) * (m * k + k * n) + 4 * m * n
+        line = {"case": f"{m}x{k}x{n}", "precision": precision, "backend": backend,
+                "median_ms": ours["median_ms"], "tflops": ours["tflops"],
+                "gbs_min_bytes": bytes_min / (ours["median_ms"] * 1e-3) / 1e9,
+                "frac_bf16_peak": ours["tflops"] / peaks["bf16_tflops"],
+                "torch_cublas_tflops": theirs["tflops"], "ratio_vs_cublas": ours["tflops"] / theirs["tflops"],
+                "max_abs_diff_vs_cublas": diff, "inputs": dist}
+        print(json.dumps(line), flush=True)
+        del a, b, c, ref, run
+    status = native.device_status()
+    native.close()
+    if status:
+        raise RuntimeError(f"device status {status:#x}")
 
 
 def single_rowshard(args) -> dict:

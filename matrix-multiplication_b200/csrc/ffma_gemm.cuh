@@ -4,14 +4,19 @@
 // Replaces the reference's FP32 kernels (matmul_tiled_fp32 / matmul_register_fp32
 // in src/matmul.cu:73-195 and matmul_warp_fp32 in src/matmul_custom.cuh:85-156)
 // with one register-blocked kernel:
-//   * 128 x 128 output tile per 256-thread block, K step 16, two blocks per SM;
+//   * 128 x 128 output tile per 256-thread block, K step 8, two blocks per SM;
 //   * each thread owns an 8 x 8 micro-tile split into 2 x 2 groups of 4 x 4 that
 //     are 64 rows / columns apart, so every shared-memory operand read is a
 //     conflict-free float4 and each warp's B reads are two 128-byte rows;
 //   * A is stored transposed (k-major) in shared memory, B as is;
-//   * the next K tile is fetched from global memory into registers while the
-//     current one is multiplied out of a double-buffered shared tile (one
-//     barrier per K step);
+//   * three levels of double buffering: the next K tile is fetched from global
+//     memory into registers, the shared tiles alternate between two buffers
+//     (one barrier per K step), and the register fragments of k-slice kk+1 are
+//     read from shared memory while the 64 FMAs of slice kk execute, so shared
+//     load latency never sits on the FFMA issue path;
+//   * the 64 multiply-adds of a k-slice are 32 packed FP32x2 FMAs (sm_100's
+//     paired FFMA: two IEEE FMAs, round to nearest, per issued instruction),
+//     so instruction issue no longer caps the FMA pipe;
 //   * float4 global loads/stores when rows are 16-byte aligned, guarded scalar
 //     accesses otherwise (offset base pointers, odd k or n, partial tiles).
 #pragma once
@@ -22,7 +27,7 @@ namespace b200 {
 
 constexpr int FF_BM = 128;
 constexpr int FF_BN = 128;
-constexpr int FF_BK = 16;
+constexpr int FF_BK = 8;
 constexpr int FF_THREADS = 256;
 
 template <bool VEC_A, bool VEC_B, bool VEC_C>
@@ -36,13 +41,17 @@ ffma_gemm_kernel(const float *__restrict__ a, const float *__restrict__ b, float
     const int tid = threadIdx.x;
     const int tx = tid & 15;                 // column group
     const int ty = tid >> 4;                 // row group
-    // Global -> shared mapping.  A: each thread loads 8 consecutive k of one row
-    // (a warp covers 32 rows with the same k offset: conflict-free transposed stores).
+    // Global -> shared mapping.  A: each thread loads kAVec float4s (consecutive k)
+    // of one row; a warp covers 32 rows at the same k offset, so the transposed
+    // shared stores are conflict-free.
+    constexpr int kAVec = FF_BK / 8;
     const int a_row = tid & 127;
-    const int a_k = (tid >> 7) * 8;
-    // B: each thread loads float4 at columns 4*(tid%16) and 64 + 4*(tid%16) of row tid/16.
-    const int b_k = tid >> 4;
-    const int b_col = (tid & 15) * 4;
+    const int a_k = (tid >> 7) * 4 * kAVec;
+    // B: each thread loads kBVec float4s of row b_k at columns b_col + 32 q
+    // (a warp covers 128 contiguous columns per store: conflict-free).
+    constexpr int kBVec = FF_BK / 8;
+    const int b_k = (tid >> 5) * kBVec;
+    const int b_col = (tid & 31) * 4;
     const int num_kt = (k + FF_BK - 1) / FF_BK;
 
     for (int block_m = blockIdx.y; block_m * FF_BM < m; block_m += gridDim.y) {
@@ -52,15 +61,14 @@ ffma_gemm_kernel(const float *__restrict__ a, const float *__restrict__ b, float
             const int grow = m0 + a_row;
             const bool a_row_ok = grow < m;
             const float *a_ptr = a + static_cast<size_t>(a_row_ok ? grow : 0) * k;
+            const int bcol = n0 + b_col;
 
-            float ra[8];
-            float rb[8];
+            float ra[4 * kAVec];
+            float rb[4 * kBVec];
             auto fetch = [&](int kt) {
-                const int kbase = kt * FF_BK;
-                // A: 8 values a[grow][kbase + a_k + 0..7]
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int kk = kbase + a_k + 4 * h;
+                for (int h = 0; h < kAVec; ++h) {
+                    const int kk = kt * FF_BK + a_k + 4 * h;
                     if (VEC_A && a_row_ok && kk + 3 < k) {
                         const float4 v = *reinterpret_cast<const float4 *>(a_ptr + kk);
                         ra[4 * h] = v.x;
@@ -73,15 +81,13 @@ ffma_gemm_kernel(const float *__restrict__ a, const float *__restrict__ b, float
                             ra[4 * h + q] = (a_row_ok && kk + q < k) ? a_ptr[kk + q] : 0.0f;
                     }
                 }
-                // B: row kbase + b_k, columns n0 + b_col + {0..3} and n0 + 64 + b_col + {0..3}
-                const int krow = kbase + b_k;
-                const bool k_ok = krow < k;
-                const float *b_ptr = b + static_cast<size_t>(k_ok ? krow : 0) * n;
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int col = n0 + b_col + 64 * h;
-                    if (VEC_B && k_ok && col + 3 < n) {
-                        const float4 v = *reinterpret_cast<const float4 *>(b_ptr + col);
+                for (int h = 0; h < kBVec; ++h) {
+                    const int krow = kt * FF_BK + b_k + h;
+                    const bool k_ok = krow < k;
+                    const float *b_ptr = b + static_cast<size_t>(k_ok ? krow : 0) * n;
+                    if (VEC_B && k_ok && bcol + 3 < n) {
+                        const float4 v = *reinterpret_cast<const float4 *>(b_ptr + bcol);
                         rb[4 * h] = v.x;
                         rb[4 * h + 1] = v.y;
                         rb[4 * h + 2] = v.z;
@@ -89,52 +95,76 @@ ffma_gemm_kernel(const float *__restrict__ a, const float *__restrict__ b, float
                     } else {
 #pragma unroll
                         for (int q = 0; q < 4; ++q)
-                            rb[4 * h + q] = (k_ok && col + q < n) ? b_ptr[col + q] : 0.0f;
+                            rb[4 * h + q] = (k_ok && bcol + q < n) ? b_ptr[bcol + q] : 0.0f;
                     }
                 }
             };
             auto stash = [&](int buf) {
 #pragma unroll
-                for (int q = 0; q < 8; ++q)
+                for (int q = 0; q < 4 * kAVec; ++q)
                     as[buf][a_k + q][a_row] = ra[q];
-                *reinterpret_cast<float4 *>(&bs[buf][b_k][b_col]) = make_float4(rb[0], rb[1], rb[2], rb[3]);
-                *reinterpret_cast<float4 *>(&bs[buf][b_k][64 + b_col]) =
-                    make_float4(rb[4], rb[5], rb[6], rb[7]);
+#pragma unroll
+                for (int h = 0; h < kBVec; ++h)
+                    *reinterpret_cast<float4 *>(&bs[buf][b_k + h][b_col]) =
+                        make_float4(rb[4 * h], rb[4 * h + 1], rb[4 * h + 2], rb[4 * h + 3]);
             };
 
-            float acc[8][8];
+            // acc[i][p] holds outputs (i, 2p) and (i, 2p + 1): one packed FP32x2 FMA
+            // (__ffma2_rn, two IEEE round-to-nearest FMAs per instruction) updates both.
+            float2 acc[8][4];
 #pragma unroll
             for (int i = 0; i < 8; ++i)
 #pragma unroll
-                for (int j = 0; j < 8; ++j)
-                    acc[i][j] = 0.0f;
+                for (int j = 0; j < 4; ++j)
+                    acc[i][j] = make_float2(0.0f, 0.0f);
+
+            float fa[2][8];
+            float fb[2][8];
+            auto load_frag = [&](int buf, int kk, int slot) {
+                const float4 a0 = *reinterpret_cast<const float4 *>(&as[buf][kk][ty * 4]);
+                const float4 a1 = *reinterpret_cast<const float4 *>(&as[buf][kk][64 + ty * 4]);
+                const float4 b0 = *reinterpret_cast<const float4 *>(&bs[buf][kk][tx * 4]);
+                const float4 b1 = *reinterpret_cast<const float4 *>(&bs[buf][kk][64 + tx * 4]);
+                fa[slot][0] = a0.x; fa[slot][1] = a0.y; fa[slot][2] = a0.z; fa[slot][3] = a0.w;
+                fa[slot][4] = a1.x; fa[slot][5] = a1.y; fa[slot][6] = a1.z; fa[slot][7] = a1.w;
+                fb[slot][0] = b0.x; fb[slot][1] = b0.y; fb[slot][2] = b0.z; fb[slot][3] = b0.w;
+                fb[slot][4] = b1.x; fb[slot][5] = b1.y; fb[slot][6] = b1.z; fb[slot][7] = b1.w;
+            };
 
             fetch(0);
             stash(0);
             __syncthreads();
+            load_frag(0, 0, 0);
             int buf = 0;
             for (int kt = 0; kt < num_kt; ++kt) {
-                if (kt + 1 < num_kt)
+                const bool more = kt + 1 < num_kt;
+                if (more)
                     fetch(kt + 1);
 #pragma unroll
                 for (int kk = 0; kk < FF_BK; ++kk) {
-                    const float4 a0 = *reinterpret_cast<const float4 *>(&as[buf][kk][ty * 4]);
-                    const float4 a1 = *reinterpret_cast<const float4 *>(&as[buf][kk][64 + ty * 4]);
-                    const float4 b0 = *reinterpret_cast<const float4 *>(&bs[buf][kk][tx * 4]);
-                    const float4 b1 = *reinterpret_cast<const float4 *>(&bs[buf][kk][64 + tx * 4]);
-                    const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-                    const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+                    const int cur = kk & 1;
+                    if (kk == FF_BK - 1) {
+                        // Publish the next tile, then read its first slice.
+                        if (more) {
+                            stash(buf ^ 1);
+                            __syncthreads();
+                            load_frag(buf ^ 1, 0, cur ^ 1);
+                        }
+                    } else {
+                        load_frag(buf, kk + 1, cur ^ 1);
+                    }
 #pragma unroll
-                    for (int i = 0; i < 8; ++i)
+                    for (int i = 0; i < 8; ++i) {
+                        const float2 ai = make_float2(fa[cur][i], fa[cur][i]);
 #pragma unroll
-                        for (int j = 0; j < 8; ++j)
-                            acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+                        for (int j = 0; j < 4; ++j)
+                            acc[i][j] = __ffma2_rn(ai, make_float2(fb[cur][2 * j], fb[cur][2 * j + 1]), acc[i][j]);
+                    }
                 }
-                if (kt + 1 < num_kt)
-                    stash(buf ^ 1);
-                __syncthreads();
                 buf ^= 1;
             }
+            // The next output tile (grid-stride case) overwrites shared buffer 0.
+            __syncthreads();
 
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
@@ -145,14 +175,169 @@ ffma_gemm_kernel(const float *__restrict__ a, const float *__restrict__ b, float
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
                     const int col = n0 + tx * 4 + 64 * h;
+                    const float2 lo = acc[i][2 * h], hi = acc[i][2 * h + 1];
                     if (VEC_C && col + 3 < n) {
-                        *reinterpret_cast<float4 *>(c_row + col) =
-                            make_float4(acc[i][4 * h], acc[i][4 * h + 1], acc[i][4 * h + 2], acc[i][4 * h + 3]);
+                        *reinterpret_cast<float4 *>(c_row + col) = make_float4(lo.x, lo.y, hi.x, hi.y);
                     } else {
+                        const float v[4] = {lo.x, lo.y, hi.x, hi.y};
 #pragma unroll
                         for (int q = 0; q < 4; ++q)
                             if (col + q < n)
-                                c_row[col + q] = acc[i][4 * h + q];
+                                c_row[col + q] = v[q];
+                    }
+                }
+            }
+        }
+    }
+}
+
+} // namespace b200
+
+namespace b200 {
+
+// ---------------------------------------------------------------------------
+// Aligned-operand variant: a 3-stage cp.async pipeline feeds shared memory
+// straight from global memory (no register staging, one barrier per 16-deep K
+// tile).  A stays row-major in shared memory (rows padded to 20 floats) and is
+// read as float4 along k, so one A fragment load serves four k-slices.  Used
+// when A and B rows are 16-byte aligned (k % 4 == 0, n % 4 == 0, aligned bases);
+// partial tiles are zero-filled by cp.async's source-size operand.
+constexpr int FA_BK = 16;
+constexpr int FA_STAGES = 3;
+constexpr int FA_A_LD = FA_BK + 4;                       // padded row of the A tile
+constexpr int FA_A_STAGE = FF_BM * FA_A_LD;              // floats
+constexpr int FA_B_STAGE = FA_BK * FF_BN;                // floats
+constexpr int FA_SMEM_BYTES = FA_STAGES * (FA_A_STAGE + FA_B_STAGE) * 4;
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, bool valid)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0)
+                 : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit()
+{
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void cp_async_wait()
+{
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <bool VEC_C>
+__global__ void __launch_bounds__(FF_THREADS, 2)
+ffma_gemm_async_kernel(const float *__restrict__ a, const float *__restrict__ b, float *__restrict__ c, int m,
+                       int n, int k)
+{
+    extern __shared__ __align__(16) float fa_smem[];
+    float *as = fa_smem;                                    // [stage][128][FA_A_LD]
+    float *bs = fa_smem + FA_STAGES * FA_A_STAGE;           // [stage][FA_BK][128]
+    const uint32_t as_addr = static_cast<uint32_t>(__cvta_generic_to_shared(as));
+    const uint32_t bs_addr = static_cast<uint32_t>(__cvta_generic_to_shared(bs));
+
+    const int tid = threadIdx.x;
+    const int tx = tid & 15;
+    const int ty = tid >> 4;
+    const int num_kt = (k + FA_BK - 1) / FA_BK;
+
+    for (int block_m = blockIdx.y; block_m * FF_BM < m; block_m += gridDim.y) {
+        for (int block_n = blockIdx.x; block_n * FF_BN < n; block_n += gridDim.x) {
+            const int m0 = block_m * FF_BM;
+            const int n0 = block_n * FF_BN;
+
+            // Tile kt -> stage s: 512 16-byte chunks of A (128 rows x 4) and of B
+            // (16 rows x 32), two of each per thread.
+            auto issue = [&](int kt, int s) {
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int chunk = tid + 256 * h;
+                    const int row = chunk >> 2, kq = chunk & 3;
+                    const int grow = m0 + row, gk = kt * FA_BK + kq * 4;
+                    const bool ok = grow < m && gk < k;
+                    const float *src = ok ? a + static_cast<size_t>(grow) * k + gk : a;
+                    cp_async16(as_addr + (s * FA_A_STAGE + row * FA_A_LD + kq * 4) * 4, src, ok);
+                }
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int chunk = tid + 256 * h;
+                    const int row = chunk >> 5, cq = chunk & 31;
+                    const int gk = kt * FA_BK + row, gcol = n0 + cq * 4;
+                    const bool ok = gk < k && gcol < n;
+                    const float *src = ok ? b + static_cast<size_t>(gk) * n + gcol : b;
+                    cp_async16(bs_addr + (s * FA_B_STAGE + row * FF_BN + cq * 4) * 4, src, ok);
+                }
+            };
+
+            float2 acc[8][4];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    acc[i][j] = make_float2(0.0f, 0.0f);
+
+#pragma unroll
+            for (int s = 0; s < FA_STAGES - 1; ++s) {
+                if (s < num_kt)
+                    issue(s, s);
+                cp_async_commit();
+            }
+            for (int kt = 0; kt < num_kt; ++kt) {
+                cp_async_wait<FA_STAGES - 2>();
+                __syncthreads();
+                const int next = kt + FA_STAGES - 1;
+                if (next < num_kt)
+                    issue(next, next % FA_STAGES);
+                cp_async_commit();
+                const float *at = as + (kt % FA_STAGES) * FA_A_STAGE;
+                const float *bt = bs + (kt % FA_STAGES) * FA_B_STAGE;
+#pragma unroll
+                for (int k4 = 0; k4 < FA_BK; k4 += 4) {
+                    float4 ar[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const int row = i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4);
+                        ar[i] = *reinterpret_cast<const float4 *>(at + row * FA_A_LD + k4);
+                    }
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) {
+                        const float4 b0 = *reinterpret_cast<const float4 *>(bt + (k4 + kk) * FF_BN + tx * 4);
+                        const float4 b1 = *reinterpret_cast<const float4 *>(bt + (k4 + kk) * FF_BN + 64 + tx * 4);
+                        const float2 bp[4] = {make_float2(b0.x, b0.y), make_float2(b0.z, b0.w),
+                                              make_float2(b1.x, b1.y), make_float2(b1.z, b1.w)};
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const float av = kk == 0 ? ar[i].x : kk == 1 ? ar[i].y : kk == 2 ? ar[i].z : ar[i].w;
+                            const float2 ai = make_float2(av, av);
+#pragma unroll
+                            for (int j = 0; j < 4; ++j)
+                                acc[i][j] = __ffma2_rn(ai, bp[j], acc[i][j]);
+                        }
+                    }
+                }
+            }
+            cp_async_wait<0>();
+            __syncthreads();
+
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int row = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
+                if (row >= m)
+                    continue;
+                float *c_row = c + static_cast<size_t>(row) * n;
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int col = n0 + tx * 4 + 64 * h;
+                    const float2 lo = acc[i][2 * h], hi = acc[i][2 * h + 1];
+                    if (VEC_C && col + 3 < n) {
+                        *reinterpret_cast<float4 *>(c_row + col) = make_float4(lo.x, lo.y, hi.x, hi.y);
+                    } else {
+                        const float v[4] = {lo.x, lo.y, hi.x, hi.y};
+#pragma unroll
+                        for (int q = 0; q < 4; ++q)
+                            if (col + q < n)
+                                c_row[col + q] = v[q];
                     }
                 }
             }

@@ -318,7 +318,17 @@ int launch_ffma(const float *a, const float *b, float *c, int m, int k, int n, c
     const bool va = aligned16(a) && k % 4 == 0;
     const bool vb = aligned16(b) && n % 4 == 0;
     const bool vc = aligned16(c) && n % 4 == 0;
-    if (va && vb && vc)
+    if (va && vb) {
+        // Aligned operands: cp.async pipeline kernel.
+        const int64_t gx = (static_cast<int64_t>(n) + FF_BN - 1) / FF_BN;
+        const int64_t gy = (static_cast<int64_t>(m) + FF_BM - 1) / FF_BM;
+        const dim3 grid(static_cast<unsigned int>(gx < 65535 ? gx : 65535),
+                        static_cast<unsigned int>(gy < 65535 ? gy : 65535));
+        if (vc)
+            ffma_gemm_async_kernel<true><<<grid, FF_THREADS, FA_SMEM_BYTES, stream>>>(a, b, c, m, n, k);
+        else
+            ffma_gemm_async_kernel<false><<<grid, FF_THREADS, FA_SMEM_BYTES, stream>>>(a, b, c, m, n, k);
+    } else if (va && vb && vc)
         launch_ffma_kernel<true, true, true>(a, b, c, m, k, n, stream);
     else if (va && vb)
         launch_ffma_kernel<true, true, false>(a, b, c, m, k, n, stream);
@@ -462,6 +472,16 @@ extern "C" void *matmul_create(int device, char *error, size_t error_size)
                                 reinterpret_cast<const void *>(&tc_gemm_kernel<kFmtTF32>)};
     for (const void *kernel : tc_kernels) {
         st = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM_BYTES);
+        if (st != cudaSuccess) {
+            delete ctx;
+            fail_cuda(error, error_size, "cudaFuncSetAttribute", st);
+            return nullptr;
+        }
+    }
+    const void *ffma_kernels[] = {reinterpret_cast<const void *>(&ffma_gemm_async_kernel<true>),
+                                  reinterpret_cast<const void *>(&ffma_gemm_async_kernel<false>)};
+    for (const void *kernel : ffma_kernels) {
+        st = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FA_SMEM_BYTES);
         if (st != cudaSuccess) {
             delete ctx;
             fail_cuda(error, error_size, "cudaFuncSetAttribute", st);
