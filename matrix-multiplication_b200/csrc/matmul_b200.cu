@@ -13,6 +13,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <utility>
 #include <new>
 
 #include "ffma_gemm.cuh"
@@ -184,15 +185,51 @@ void prepare_operand(int prec, const void *src, int64_t rows, int64_t cols, bool
     }
 }
 
+// tile_n selects the kernel: 0 = CTA pair (256 x 256), else the single-CTA
+// kernel with a 128 x tile_n tile.
 template <int FMT>
-cudaError_t launch_tc_kernel(bool pair, const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &mc,
+cudaError_t launch_tc_kernel(int tile_n, const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &mc,
                              const TcParams &params, int grid, cudaStream_t stream)
 {
-    if (pair)
+    if (tile_n == 0)
         tc2_gemm_kernel<FMT><<<grid, TC_THREADS, TC2_SMEM_BYTES, stream>>>(ma, mb, mc, params);
+    else if (tile_n == 256)
+        tc_gemm_kernel<FMT, 256><<<grid, TC_THREADS, TcTile<256>::kSmem, stream>>>(ma, mb, mc, params);
+    else if (tile_n == 128)
+        tc_gemm_kernel<FMT, 128><<<grid, TC_THREADS, TcTile<128>::kSmem, stream>>>(ma, mb, mc, params);
+    else if (params.a_box_rows <= 32)
+        tc_gemm_kernel<FMT, 64, 32><<<grid, TC_THREADS, TcTile<64, 32>::kSmem, stream>>>(ma, mb, mc, params);
     else
-        tc_gemm_kernel<FMT><<<grid, TC_THREADS, TC_SMEM_BYTES, stream>>>(ma, mb, mc, params);
+        tc_gemm_kernel<FMT, 64><<<grid, TC_THREADS, TcTile<64>::kSmem, stream>>>(ma, mb, mc, params);
     return cudaGetLastError();
+}
+
+// Kernel choice: estimated time = rounds of tiles over the resident CTAs (or
+// CTA pairs) x per-SM tile work / relative efficiency of the tile shape (wider
+// tiles stage fewer operand bytes per FLOP).  The CTA pair needs m > 128.
+int choose_tile_n(const Context *ctx, int m, int n)
+{
+    const int64_t rows = (m + TC_BM - 1) / TC_BM;
+    double best = 0.0;
+    int choice = 64;
+    for (int tile_n : {256, 128, 64}) {
+        const double efficiency = tile_n == 256 ? 0.95 : tile_n == 128 ? 0.85 : 0.7;
+        const int64_t tiles = rows * ((n + tile_n - 1) / tile_n);
+        const double cost = static_cast<double>((tiles + ctx->sm_count - 1) / ctx->sm_count) * TC_BM * tile_n /
+                            efficiency;
+        if (best == 0.0 || cost < best) {
+            best = cost;
+            choice = tile_n;
+        }
+    }
+    if (m > TC_BM && ctx->max_pairs > 0) {
+        const int64_t pair_tiles = ((m + TC2_BM - 1) / TC2_BM) * static_cast<int64_t>((n + TC2_BN - 1) / TC2_BN);
+        const double cost = static_cast<double>((pair_tiles + ctx->max_pairs - 1) / ctx->max_pairs) *
+                            (TC2_BM / 2) * TC2_BN;
+        if (cost <= best)
+            choice = 0;
+    }
+    return choice;
 }
 
 int launch_tcgen05(Context *ctx, int prec, const void *a, const void *b, float *c, int m, int k, int n,
@@ -237,21 +274,23 @@ int launch_tcgen05(Context *ctx, int prec, const void *a, const void *b, float *
     else
         prepare_operand(prec, b, k, n, b_direct, const_cast<void *>(b_op), ldb, ctx, stream);
 
-    // CTA pairs (256 x 256 tiles) whenever there is more than one 128-row block.
-    const bool pair = m > TC_BM && ctx->max_pairs > 0;
+    const int kernel_n = choose_tile_n(ctx, m, n);
+    const bool pair = kernel_n == 0;
     const int tile_m = pair ? TC2_BM : TC_BM;
-    const int tile_n = pair ? TC2_BN : TC_BN;
+    const int tile_n = pair ? TC2_BN : kernel_n;
     const CUtensorMapDataType type = prec == kPrecTf32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                      : prec == kPrecBf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                          : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     const uint32_t bk = TC_ROW_BYTES / elem;
     alignas(64) CUtensorMap map_a, map_b, map_c;
     std::memset(&map_c, 0, sizeof(map_c));
+    // Skinny problems (m < 128) fetch only the rows that exist.
+    const int a_box_rows = pair || m >= TC_BM ? TC_BM : static_cast<int>(round_up(m, 16));
     bool ok = encode_2d(ctx, &map_a, type, a_op, static_cast<uint64_t>(k), static_cast<uint64_t>(m),
-                        static_cast<uint64_t>(lda) * elem, bk, TC_BM);
+                        static_cast<uint64_t>(lda) * elem, bk, static_cast<uint32_t>(a_box_rows));
     if (b_transposed)
         ok = ok && encode_2d(ctx, &map_b, type, b_op, static_cast<uint64_t>(k), static_cast<uint64_t>(n),
-                             static_cast<uint64_t>(ldb) * elem, bk, pair ? TC2_HALF : TC_BN);
+                             static_cast<uint64_t>(ldb) * elem, bk, pair ? TC2_HALF : tile_n);
     else
         ok = ok && encode_2d(ctx, &map_b, type, b_op, static_cast<uint64_t>(n), static_cast<uint64_t>(k),
                              static_cast<uint64_t>(ldb) * elem, TC_ROW_BYTES / elem, bk);
@@ -285,16 +324,17 @@ int launch_tcgen05(Context *ctx, int prec, const void *a, const void *b, float *
     params.group_m = pair ? kRasterGroupMPair : kRasterGroupM;
     params.c = c;
     params.c_direct = c_direct ? 1 : 0;
+    params.a_box_rows = a_box_rows;
     const int units = pair ? ctx->max_pairs : ctx->sm_count;
     const int grid = static_cast<int>(tiles < units ? tiles : units) * (pair ? 2 : 1);
 
     cudaError_t st;
     if (prec == kPrecTf32)
-        st = launch_tc_kernel<kFmtTF32>(pair, map_a, map_b, map_c, params, grid, stream);
+        st = launch_tc_kernel<kFmtTF32>(kernel_n, map_a, map_b, map_c, params, grid, stream);
     else if (prec == kPrecBf16)
-        st = launch_tc_kernel<kFmtBF16>(pair, map_a, map_b, map_c, params, grid, stream);
+        st = launch_tc_kernel<kFmtBF16>(kernel_n, map_a, map_b, map_c, params, grid, stream);
     else
-        st = launch_tc_kernel<kFmtF16>(pair, map_a, map_b, map_c, params, grid, stream);
+        st = launch_tc_kernel<kFmtF16>(kernel_n, map_a, map_b, map_c, params, grid, stream);
     if (pooled)
         cudaFreeAsync(pooled, stream);
     if (st != cudaSuccess)
@@ -394,13 +434,13 @@ extern "C" int matmul_kernel_info(int implementation, int precision, char *json,
             "\"accumulator\":\"tmem_fp32\",\"tmem_columns\":%u,\"accumulator_buffers\":2,"
             "\"warp_roles\":{\"tma\":1,\"mma\":1,\"epilogue\":4},\"schedule\":\"persistent\","
             "\"raster_group_m\":%d,\"epilogue\":\"tmem_ld_smem_tma_store\",\"input_rounding\":\"%s\","
-            "\"b_operand\":\"%s\",\"small_m_kernel\":{\"max_m\":%d,\"cta_group\":1,\"tile_m\":%d,"
-            "\"tile_n\":%d,\"buffering\":%d,\"raster_group_m\":%d}}",
+            "\"b_operand\":\"%s\",\"single_cta_kernel\":{\"when\":\"pair tiles < one wave\",\"tile_m\":%d,"
+            "\"tile_n\":[256,128,64],\"buffering\":[%d,%d,%d],\"raster_group_m\":%d}}",
             kPrecisionNames[precision], TC2_BM, TC2_BN, TC_ROW_BYTES / elem, TC_THREADS, TC2_HALF, TC2_BN, TC2_HALF,
             TC2_BN, TC2_STAGES, precision == kPrecTf32 ? "tf32" : "f16", TC2_BM, TC2_BN, 32 / elem,
             TC_TMEM_COLUMNS, kRasterGroupMPair, precision == kPrecTf32 ? "rne_prepass" : "none",
-            precision == kPrecTf32 ? "k_major_rounded_transpose" : "mn_major_tma", TC_BM, TC_BM, TC_BN, TC_STAGES,
-            kRasterGroupM);
+            precision == kPrecTf32 ? "k_major_rounded_transpose" : "mn_major_tma", TC_BM, TcTile<256>::kStages,
+            TcTile<128>::kStages, TcTile<64>::kStages, kRasterGroupM);
     } else {
         written = std::snprintf(
             json, json_size,
@@ -467,11 +507,21 @@ extern "C" void *matmul_create(int device, char *error, size_t error_size)
     }
     ctx->encode = reinterpret_cast<EncodeTiledFn>(fn);
 
-    const void *tc_kernels[] = {reinterpret_cast<const void *>(&tc_gemm_kernel<kFmtF16>),
-                                reinterpret_cast<const void *>(&tc_gemm_kernel<kFmtBF16>),
-                                reinterpret_cast<const void *>(&tc_gemm_kernel<kFmtTF32>)};
-    for (const void *kernel : tc_kernels) {
-        st = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM_BYTES);
+    const std::pair<const void *, int> tc_kernels[] = {
+        {reinterpret_cast<const void *>(&tc_gemm_kernel<kFmtF16, 256>), TcTile<256>::kSmem},
+        {reinterpret_cast<const void *>(&tc_gemm_kernel<kFmtBF16, 256>), TcTile<256>::kSmem},
+        {reinterpret_cast<const void *>(&tc_gemm_kernel<kFmtTF32, 256>), TcTile<256>::kSmem},
+        {reinterpret_cast<const void *>(&tc_gemm_kernel<kFmtF16, 128>), TcTile<128>::kSmem},
+        {reinterpret_cast<const void *>(&tc_gemm_kernel<kFmtBF16, 128>), TcTile<128>::kSmem},
+        {reinterpret_cast<const void *>(&tc_gemm_kernel<kFmtTF32, 128>), TcTile<128>::kSmem},
+        {reinterpret_cast<const void *>(&tc_gemm_kernel<kFmtF16, 64>), TcTile<64>::kSmem},
+        {reinterpret_cast<const void *>(&tc_gemm_kernel<kFmtBF16, 64>), TcTile<64>::kSmem},
+        {reinterpret_cast<const void *>(&tc_gemm_kernel<kFmtTF32, 64>), TcTile<64>::kSmem},
+        {reinterpret_cast<const void *>(&tc_gemm_kernel<kFmtF16, 64, 32>), TcTile<64, 32>::kSmem},
+        {reinterpret_cast<const void *>(&tc_gemm_kernel<kFmtBF16, 64, 32>), TcTile<64, 32>::kSmem},
+        {reinterpret_cast<const void *>(&tc_gemm_kernel<kFmtTF32, 64, 32>), TcTile<64, 32>::kSmem}};
+    for (const auto &kernel : tc_kernels) {
+        st = cudaFuncSetAttribute(kernel.first, cudaFuncAttributeMaxDynamicSharedMemorySize, kernel.second);
         if (st != cudaSuccess) {
             delete ctx;
             fail_cuda(error, error_size, "cudaFuncSetAttribute", st);

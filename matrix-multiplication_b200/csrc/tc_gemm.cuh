@@ -4,7 +4,9 @@
 // Replaces the reference's matmul_wmma<T,BK> (src/matmul_custom.cuh:169-235),
 // which staged scalars through shared memory into mma.sync fragments.  Here:
 //
-//   warp 0      TMA producer: one elected lane streams A (128 x 128 B) and
+//   warp 0      TMA producer: one elected lane streams A (up to 128 x 128 B;
+//               for m < 128 only the first m rows rounded up to 16, the MMA's
+//               other rows hold stale data whose outputs are never stored) and
 //               B (128 B-wide column blocks) boxes into a 4-stage ring with
 //               128-byte swizzle, signalling a "full" mbarrier per stage.
 //   warp 1      TMEM owner + MMA issuer: allocates 512 TMEM columns (two
@@ -59,10 +61,26 @@ constexpr int TC_A_STAGE = TC_BM * TC_ROW_BYTES;   // 16 KB
 constexpr int TC_B_STAGE = TC_BN * TC_ROW_BYTES;   // 32 KB (BK rows x BN elements)
 constexpr int TC_EPI_BOX = 32 * 32 * 4;            // 32 rows x 32 FP32 columns
 constexpr int TC_EPI_BYTES = 4 * 2 * TC_EPI_BOX;   // 4 warps, double buffered
-constexpr int TC_BAR_BYTES = 256;
+constexpr int TC_BAR_BYTES = 512;
 constexpr int TC_SMEM_BYTES =
     1024 /* alignment slack */ + TC_STAGES * (TC_A_STAGE + TC_B_STAGE) + TC_EPI_BYTES + TC_BAR_BYTES;
 constexpr uint32_t TC_TMEM_COLUMNS = 2 * TC_BN;
+
+// Geometry of the single-CTA kernel for a tile width BN (256, 128 or 64) and an
+// A stage of AROWS rows (128, or 32 for m <= 32): the narrower tiles give small
+// and skinny problems more CTAs, and the smaller stages buy a deeper ring in the
+// same ~225 KB of shared memory (16 stages, 128 KB of B in flight per SM, for
+// the skinny, HBM-bound case).
+template <int BN, int AROWS = 128>
+struct TcTile {
+    static_assert(BN == 256 || BN == 128 || BN == 64, "tile width");
+    static_assert(AROWS == 128 || AROWS == 32, "A stage rows");
+    static constexpr int kAStage = AROWS * TC_ROW_BYTES;
+    static constexpr int kBStage = BN * TC_ROW_BYTES;
+    static constexpr int kStages = AROWS == 32 ? 16 : BN == 256 ? 4 : BN == 128 ? 6 : 8;
+    static constexpr int kSmem = 1024 + kStages * (kAStage + kBStage) + TC_EPI_BYTES + TC_BAR_BYTES;
+    static constexpr uint32_t kTmemColumns = 2 * BN;   // two accumulators
+};
 
 struct TcParams {
     int m, n, k;
@@ -71,6 +89,7 @@ struct TcParams {
     int group_m;     // M-blocks per raster group
     float *c;        // output (direct-store epilogue only)
     int c_direct;    // 1 when C cannot be written by TMA
+    int a_box_rows;  // rows per A box (single-CTA kernel: m rounded up to 16 when m < 128)
 };
 
 // Instruction descriptor (kind::f16 / kind::tf32): FP32 accumulator (bits 4-5 = 1),
@@ -94,42 +113,47 @@ __device__ __forceinline__ void tc_tile_coords(int tile, const TcParams &p, int 
     nb = local / rows;
 }
 
-template <int FMT>
+template <int FMT, int BN, int AROWS = 128>
 __global__ void __launch_bounds__(TC_THREADS, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                const __grid_constant__ CUtensorMap map_c, const TcParams p)
 {
+    using Tile = TcTile<BN, AROWS>;
+    constexpr int kStages = Tile::kStages;
+    constexpr int kAStage = Tile::kAStage;
+    constexpr int kBStage = Tile::kBStage;
+    constexpr uint32_t kTmemColumns = Tile::kTmemColumns;
     constexpr bool kTF32 = FMT == kFmtTF32;
     constexpr int kElem = kTF32 ? 4 : 2;
     constexpr int kBK = TC_ROW_BYTES / kElem;          // K elements per stage (64 or 32)
     constexpr int kMmaK = 32 / kElem;                  // K per instruction (16 or 8)
     constexpr int kMmasPerStage = kBK / kMmaK;         // 4
     constexpr int kNB = TC_ROW_BYTES / kElem;          // B box width in elements (64 or 32)
-    constexpr int kBBoxes = TC_BN / kNB;               // 4 or 8
+    constexpr int kBBoxes = BN / kNB;                  // MN-major B boxes per stage
     constexpr uint32_t kBBoxBytes = kBK * TC_ROW_BYTES;  // bytes per B column block
     constexpr bool kBKMajor = kTF32;                     // TF32 B arrives transposed
-    constexpr uint32_t kIdesc = tc_instr_desc(FMT, kBKMajor);
+    constexpr uint32_t kIdesc = tc_instr_desc(FMT, kBKMajor, TC_BM, BN);
 
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_addr(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
     const uint32_t s_a = base;
-    const uint32_t s_b = s_a + TC_STAGES * TC_A_STAGE;
-    const uint32_t s_epi = s_b + TC_STAGES * TC_B_STAGE;
+    const uint32_t s_b = s_a + kStages * kAStage;
+    const uint32_t s_epi = s_b + kStages * kBStage;
     const uint32_t s_bar = s_epi + TC_EPI_BYTES;
     auto full_bar = [&](int s) { return s_bar + 8u * s; };
-    auto empty_bar = [&](int s) { return s_bar + 8u * (TC_STAGES + s); };
-    auto accf_bar = [&](int i) { return s_bar + 8u * (2 * TC_STAGES + i); };
-    auto acce_bar = [&](int i) { return s_bar + 8u * (2 * TC_STAGES + 2 + i); };
-    const uint32_t drain_bar = s_bar + 8u * (2 * TC_STAGES + 4);
-    const uint32_t tmem_slot = s_bar + 8u * (2 * TC_STAGES + 5);
+    auto empty_bar = [&](int s) { return s_bar + 8u * (kStages + s); };
+    auto accf_bar = [&](int i) { return s_bar + 8u * (2 * kStages + i); };
+    auto acce_bar = [&](int i) { return s_bar + 8u * (2 * kStages + 2 + i); };
+    const uint32_t drain_bar = s_bar + 8u * (2 * kStages + 4);
+    const uint32_t tmem_slot = s_bar + 8u * (2 * kStages + 5);
     uint32_t *tmem_slot_ptr = reinterpret_cast<uint32_t *>(smem_raw + (tmem_slot - raw));
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < TC_STAGES; ++s) {
+        for (int s = 0; s < kStages; ++s) {
             mbar_init(full_bar(s), 1);
             mbar_init(empty_bar(s), 1);
         }
@@ -147,7 +171,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             tma_prefetch_map(&map_c);
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, TC_TMEM_COLUMNS);
+        tmem_alloc(tmem_slot, kTmemColumns);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -171,27 +195,27 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(full_bar(stage), TC_A_STAGE + TC_B_STAGE);
-                    tma_load_2d(s_a + stage * TC_A_STAGE, &map_a, full_bar(stage), kb * kBK, mb * TC_BM);
+                    mbar_arrive_expect_tx(full_bar(stage), p.a_box_rows * TC_ROW_BYTES + kBStage);
+                    tma_load_2d(s_a + stage * kAStage, &map_a, full_bar(stage), kb * kBK, mb * TC_BM);
                     if constexpr (kBKMajor) {
-                        // B^T tile: TC_BN rows (n) x 128 bytes (k), one box.
-                        tma_load_2d(s_b + stage * TC_B_STAGE, &map_b, full_bar(stage), kb * kBK, nb * TC_BN);
+                        // B^T tile: BN rows (n) x 128 bytes (k), one box.
+                        tma_load_2d(s_b + stage * kBStage, &map_b, full_bar(stage), kb * kBK, nb * BN);
                     } else {
 #pragma unroll
                         for (int j = 0; j < kBBoxes; ++j)
-                            tma_load_2d(s_b + stage * TC_B_STAGE + j * kBBoxBytes, &map_b, full_bar(stage),
-                                        nb * TC_BN + j * kNB, kb * kBK);
+                            tma_load_2d(s_b + stage * kBStage + j * kBBoxBytes, &map_b, full_bar(stage),
+                                        nb * BN + j * kNB, kb * kBK);
                     }
                     filled |= 1u << stage;
                     fill_parity = (fill_parity & ~(1u << stage)) | (phase << stage);
-                    if (++stage == TC_STAGES) {
+                    if (++stage == kStages) {
                         stage = 0;
                         phase ^= 1u;
                     }
                 }
             }
             // Let every issued copy land before the CTA can exit.
-            for (int s = 0; s < TC_STAGES; ++s)
+            for (int s = 0; s < kStages; ++s)
                 if ((filled >> s) & 1u)
                     if (!mbar_wait(full_bar(s), (fill_parity >> s) & 1u))
                         report_status(kStatusDrainTimeout);
@@ -206,8 +230,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             // address >> 4) moves between stages and K slices, so the issue loop adds.
             const uint64_t a_desc0 = smem_desc_sw128(s_a, 16, 1024);
             const uint64_t b_desc0 = kBKMajor ? smem_desc_sw128(s_b, 16, 1024) : smem_desc_sw128(s_b, kBBoxBytes, 1024);
-            constexpr uint64_t kADescStage = TC_A_STAGE >> 4;
-            constexpr uint64_t kBDescStage = TC_B_STAGE >> 4;
+            constexpr uint64_t kADescStage = kAStage >> 4;
+            constexpr uint64_t kBDescStage = kBStage >> 4;
             constexpr uint64_t kADescK = 32 >> 4;
             constexpr uint64_t kBDescK = kBKMajor ? (32 >> 4) : ((kMmaK * TC_ROW_BYTES) >> 4);
             int acc = 0;
@@ -219,7 +243,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                     break;
                 }
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * TC_BN);
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
                 for (int kb = 0; kb < p.num_k_blocks; ++kb) {
                     if (!mbar_wait(full_bar(stage), phase)) {
                         report_status(kStatusMmaTimeout);
@@ -234,7 +258,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                         tc_mma<kTF32>(d_tmem, a_desc + kk * kADescK, b_desc + kk * kBDescK, kIdesc,
                                       (kb | kk) != 0 ? 1u : 0u);
                     tc_commit(empty_bar(stage));
-                    if (++stage == TC_STAGES) {
+                    if (++stage == kStages) {
                         stage = 0;
                         phase ^= 1u;
                     }
@@ -275,16 +299,16 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             tc_fence_after();
             const int row0 = mb * TC_BM + quarter * 32;
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
-                                   static_cast<uint32_t>(acc * TC_BN);
+                                   static_cast<uint32_t>(acc * BN);
 #pragma unroll 1
-            for (int chunk = 0; chunk < TC_BN / 32; ++chunk) {
+            for (int chunk = 0; chunk < BN / 32; ++chunk) {
                 uint32_t v[32];
                 tmem_load_32cols(t_row + chunk * 32, v);
-                if (chunk == TC_BN / 32 - 1) {
+                if (chunk == BN / 32 - 1) {
                     tc_fence_before();
                     mbar_arrive(acce_bar(acc));
                 }
-                const int col0 = nb * TC_BN + chunk * 32;
+                const int col0 = nb * BN + chunk * 32;
                 if (col0 >= p.n || row0 >= p.m)
                     continue;
                 if (!p.c_direct) {
@@ -329,7 +353,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, TC_TMEM_COLUMNS);
+        tmem_dealloc(tmem_base, kTmemColumns);
     }
 }
 

@@ -36,7 +36,11 @@ ROOT = Path(__file__).resolve().parents[1]
 REFERENCE_SHAPES = ((1, 1, 1), (7, 13, 11), (35, 37, 67), (129, 35, 133), (2, 2049, 3))
 RAGGED_SHAPES = ((31, 33, 65), (511, 257, 129), (513, 129, 577))
 EDGE_SHAPES = ((128, 64, 256), (129, 65, 257), (255, 127, 255), (300, 1000, 520), (17, 65, 19), (3, 2049, 5))
-ALIGNED_SHAPES = ((128, 64, 256), (256, 512, 512), (384, 192, 768), (1000, 1024, 1000), (640, 4096, 264))
+ALIGNED_SHAPES = ((128, 64, 256), (256, 512, 512), (384, 192, 768), (1000, 1024, 1000), (640, 4096, 264),
+                  # one shape per tcgen05 kernel choice: single-CTA 256-, 128-, 64-wide tiles, CTA pairs
+                  (100, 64, 37888), (64, 128, 16384), (300, 96, 300), (2048, 128, 2048), (1024, 256, 4864),
+                  # skinny: 16-row A boxes into 32-row stages, 16-deep ring
+                  (16, 512, 8192), (32, 1024, 4096))
 PLANS = [(backend, precision) for backend in ("tcgen05", "ffma") for precision in BACKEND_PRECISIONS[backend]]
 
 
@@ -417,3 +421,21 @@ def test_reference_library_agrees(native):
         assert difference <= 2 * float(reference.roundoff_bound.max()) + 1e-3
     reference.verify(ours.cpu().numpy(), "tcgen05")
     lib.matmul_destroy(ctx, err, len(err))
+
+
+@pytest.mark.parametrize("precision,chunks", [("bf16", 4), ("tf32", 3), ("fp32", 2), ("fp16", 1)])
+def test_host_to_host_pipeline(native, precision, chunks):
+    """end_to_end.HostMatmul: FP32 host inputs, on-device conversion, chunked GEMM
+    and overlapped copies give the oracle's answer in a pinned host buffer."""
+    from end_to_end import HostMatmul
+
+    m, k, n = 1000, 384, 520
+    a_np = po.seeded_uniform((m, k), 41)
+    b_np = po.seeded_uniform((k, n), 42)
+    host_gemm = HostMatmul(native, m, k, n, precision, chunks=chunks)
+    a = torch.from_numpy(a_np).pin_memory()
+    b = torch.from_numpy(b_np).pin_memory()
+    c = torch.full((m, n), float("nan"), dtype=torch.float32).pin_memory()
+    for _ in range(2):
+        host_gemm(a, b, c)
+        po.GemmReference(a_np, b_np, precision).verify(c.numpy(), f"host pipeline {precision}")
