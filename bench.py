@@ -312,7 +312,7 @@ def single_gpu(args) -> dict:
     traffic = None
     traffic_file = ROOT / "profiles" / "ncu_traffic.json"
     if traffic_file.exists():
-        traffic = json.loads(traffic_file.read_text()).get("tc_gemm_bf16_8192")
+        traffic = json.loads(traffic_file.read_text()).get("tc2_gemm_bf16_8192")
     peak = peaks["bf16_tflops"]
     return {
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
@@ -326,7 +326,7 @@ def single_gpu(args) -> dict:
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "traffic": traffic,
                      "peak_source": f"{peak_kind} bf16_tflops (burst, cuBLAS 8192^3)",
-                     "kernel": "tc_gemm_kernel<BF16>", "kernel_ms": kernel_ms,
+                     "kernel": "tc2_gemm_kernel<BF16> (CTA pairs)", "kernel_ms": kernel_ms,
                      "algorithmic_flops_per_launch": 2.0 * m * k * n},
         "cpu_baseline": cpu_baseline(),
         "e2e": e2e,
