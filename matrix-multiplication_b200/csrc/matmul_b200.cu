@@ -20,6 +20,7 @@
 #include "pack.cuh"
 #include "tc_gemm.cuh"
 #include "tc2_gemm.cuh"
+#include "tc_skinny.cuh"
 
 // Scratch for matmul_launch_noalloc: a fixed array in the module's device
 // memory, so that entry point never allocates.  Every GPU that loads this
@@ -60,6 +61,7 @@ constexpr int kImplFfma = 8;
 constexpr int kPrecFp32 = 0, kPrecTf32 = 1, kPrecFp16 = 2, kPrecBf16 = 3;
 constexpr int kRasterGroupM = 16;
 constexpr int kRasterGroupMPair = 8;
+constexpr int kSkinnyMaxM = 64;        // m <= 64: swap-AB skinny kernel
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                    const cuuint64_t *, const cuuint32_t *, const cuuint32_t *,
@@ -232,6 +234,81 @@ int choose_tile_n(const Context *ctx, int m, int n)
     return choice;
 }
 
+template <int FMT, int NP>
+cudaError_t launch_skinny_kernel(const CUtensorMap &mbt, const CUtensorMap &mat, const SkParams &params, int grid,
+                                 cudaStream_t stream)
+{
+    tc_skinny_kernel<FMT, NP><<<grid, TC_THREADS, SkTile<NP>::kSmem, stream>>>(mbt, mat, params);
+    return cudaGetLastError();
+}
+
+template <int FMT>
+cudaError_t launch_skinny_np(int np, const CUtensorMap &mbt, const CUtensorMap &mat, const SkParams &params,
+                             int grid, cudaStream_t stream)
+{
+    if (np == 16)
+        return launch_skinny_kernel<FMT, 16>(mbt, mat, params, grid, stream);
+    if (np == 32)
+        return launch_skinny_kernel<FMT, 32>(mbt, mat, params, grid, stream);
+    return launch_skinny_kernel<FMT, 64>(mbt, mat, params, grid, stream);
+}
+
+// m <= 64: C^T = B^T A^T with N on the MMA's 128-row side (tc_skinny.cuh).  The
+// operands are already in TMA-ready form (a_op: m x lda; b_op: k x ldb, or for
+// TF32 the rounded transpose n x ldb).
+int launch_skinny(Context *ctx, int prec, const void *a_op, int64_t lda, const void *b_op, int64_t ldb,
+                  bool b_transposed, float *c, int m, int k, int n, cudaStream_t stream, char *error,
+                  size_t error_size)
+{
+    const int elem = prec == kPrecTf32 ? 4 : 2;
+    const uint32_t bk = TC_ROW_BYTES / elem;
+    const int np = m <= 16 ? 16 : m <= 32 ? 32 : 64;
+    const CUtensorMapDataType type = prec == kPrecTf32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                     : prec == kPrecBf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                         : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    alignas(64) CUtensorMap map_bt, map_at;
+    bool ok;
+    if (b_transposed)
+        ok = encode_2d(ctx, &map_bt, type, b_op, static_cast<uint64_t>(k), static_cast<uint64_t>(n),
+                       static_cast<uint64_t>(ldb) * elem, bk, SK_BM);
+    else
+        ok = encode_2d(ctx, &map_bt, type, b_op, static_cast<uint64_t>(n), static_cast<uint64_t>(k),
+                       static_cast<uint64_t>(ldb) * elem, TC_ROW_BYTES / elem, bk);
+    ok = ok && encode_2d(ctx, &map_at, type, a_op, static_cast<uint64_t>(k), static_cast<uint64_t>(m),
+                         static_cast<uint64_t>(lda) * elem, bk, static_cast<uint32_t>(np));
+    if (!ok) {
+        cudaGetLastError();
+        return fail(error, error_size, "matmul_launch", "cuTensorMapEncodeTiled rejected an operand");
+    }
+    SkParams params{};
+    params.m = m;
+    params.n = n;
+    params.k = k;
+    params.num_n_tiles = (n + SK_BM - 1) / SK_BM;
+    params.total_k_blocks = static_cast<int>((static_cast<int64_t>(k) + bk - 1) / bk);
+    // Two K halves when the column slabs alone would leave half the SMs idle.
+    params.splits = (2 * params.num_n_tiles <= ctx->sm_count && params.total_k_blocks >= 4) ? 2 : 1;
+    params.num_k_blocks = (params.total_k_blocks + params.splits - 1) / params.splits;
+    params.num_tiles = params.num_n_tiles * params.splits;
+    params.c = c;
+    if (params.splits > 1) {
+        const cudaError_t st = cudaMemsetAsync(c, 0, static_cast<size_t>(m) * n * sizeof(float), stream);
+        if (st != cudaSuccess)
+            return fail_cuda(error, error_size, "matmul_launch: cudaMemsetAsync", st);
+    }
+    const int grid = params.num_tiles < ctx->sm_count ? params.num_tiles : ctx->sm_count;
+    cudaError_t st;
+    if (prec == kPrecTf32)
+        st = launch_skinny_np<kFmtTF32>(np, map_bt, map_at, params, grid, stream);
+    else if (prec == kPrecBf16)
+        st = launch_skinny_np<kFmtBF16>(np, map_bt, map_at, params, grid, stream);
+    else
+        st = launch_skinny_np<kFmtF16>(np, map_bt, map_at, params, grid, stream);
+    if (st != cudaSuccess)
+        return fail(error, error_size, "kernel launch", cudaGetErrorString(st));
+    return 0;
+}
+
 int launch_tcgen05(Context *ctx, int prec, const void *a, const void *b, float *c, int m, int k, int n,
                    cudaStream_t stream, char *error, size_t error_size, void *fixed_scratch = nullptr,
                    size_t fixed_scratch_bytes = 0)
@@ -273,6 +350,14 @@ int launch_tcgen05(Context *ctx, int prec, const void *a, const void *b, float *
         transpose_round_b(b, const_cast<void *>(b_op), k, n, ldb, stream);
     else
         prepare_operand(prec, b, k, n, b_direct, const_cast<void *>(b_op), ldb, ctx, stream);
+
+    if (m <= kSkinnyMaxM) {
+        const int rc = launch_skinny(ctx, prec, a_op, lda, b_op, ldb, b_transposed, c, m, k, n, stream, error,
+                                     error_size);
+        if (pooled)
+            cudaFreeAsync(pooled, stream);
+        return rc;
+    }
 
     const int kernel_n = choose_tile_n(ctx, m, n);
     const bool pair = kernel_n == 0;
@@ -532,6 +617,24 @@ extern "C" void *matmul_create(int device, char *error, size_t error_size)
                                   reinterpret_cast<const void *>(&ffma_gemm_async_kernel<false>)};
     for (const void *kernel : ffma_kernels) {
         st = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FA_SMEM_BYTES);
+        if (st != cudaSuccess) {
+            delete ctx;
+            fail_cuda(error, error_size, "cudaFuncSetAttribute", st);
+            return nullptr;
+        }
+    }
+    const std::pair<const void *, int> skinny_kernels[] = {
+        {reinterpret_cast<const void *>(&tc_skinny_kernel<kFmtF16, 16>), SkTile<16>::kSmem},
+        {reinterpret_cast<const void *>(&tc_skinny_kernel<kFmtBF16, 16>), SkTile<16>::kSmem},
+        {reinterpret_cast<const void *>(&tc_skinny_kernel<kFmtTF32, 16>), SkTile<16>::kSmem},
+        {reinterpret_cast<const void *>(&tc_skinny_kernel<kFmtF16, 32>), SkTile<32>::kSmem},
+        {reinterpret_cast<const void *>(&tc_skinny_kernel<kFmtBF16, 32>), SkTile<32>::kSmem},
+        {reinterpret_cast<const void *>(&tc_skinny_kernel<kFmtTF32, 32>), SkTile<32>::kSmem},
+        {reinterpret_cast<const void *>(&tc_skinny_kernel<kFmtF16, 64>), SkTile<64>::kSmem},
+        {reinterpret_cast<const void *>(&tc_skinny_kernel<kFmtBF16, 64>), SkTile<64>::kSmem},
+        {reinterpret_cast<const void *>(&tc_skinny_kernel<kFmtTF32, 64>), SkTile<64>::kSmem}};
+    for (const auto &kernel : skinny_kernels) {
+        st = cudaFuncSetAttribute(kernel.first, cudaFuncAttributeMaxDynamicSharedMemorySize, kernel.second);
         if (st != cudaSuccess) {
             delete ctx;
             fail_cuda(error, error_size, "cudaFuncSetAttribute", st);

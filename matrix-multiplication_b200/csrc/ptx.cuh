@@ -327,6 +327,20 @@ __device__ __forceinline__ void tma_store_2d_hint(const void *map, uint32_t src,
         : "memory");
 }
 
+// 16 consecutive FP32 columns of this thread's TMEM lane, waited in the same asm block.
+__device__ __forceinline__ void tmem_load_16cols(uint32_t taddr, uint32_t (&v)[16])
+{
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
+          "=r"(v[15])
+        : "r"(taddr)
+        : "memory");
+}
+
 // Shared-memory matrix descriptor for tcgen05.mma (sm_100 format, version 1):
 // start address, leading- and stride-dimension byte offsets (all >> 4) and the
 // 128-byte swizzle layout (type 2 in bits 61-63).

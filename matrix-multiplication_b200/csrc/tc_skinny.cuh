@@ -1,0 +1,273 @@
+// Skinny GEMM (m <= 64): C = A * B computed as C^T = B^T * A^T on the tensor cores.
+//
+// With only a handful of rows the GEMM is HBM-bound on B (16 x 8192 x 8192 BF16
+// reads 134 MB of B for 2.1 GFLOP).  Putting N on the MMA's 128-row side keeps
+// the tensor core busy on useful work and lets each CTA stream a 128-column slab
+// of B in 256-byte row segments:
+//   * MMA "A" operand = B^T (128 columns n x 64 k per stage): for FP16/BF16 read
+//     straight from row-major B as the MN-major operand (two 64-column TMA boxes);
+//     for TF32 from the rounded, transposed copy (K-major, one box).
+//   * MMA "B" operand = A^T (NP rows m x 64 k, K-major): NP = m rounded up to 16,
+//     32 or 64.
+//   * TMEM: 128 lanes (n) x NP columns (m), two accumulators.
+//   * Epilogue: each warp loads 16 columns (m) of its 32 lanes (n) and writes, per
+//     m, 32 consecutive floats of C's row m (one 128-byte store per warp per row).
+//   * Split K in two when there are too few 128-column slabs to occupy the GPU:
+//     both halves add into a zeroed C with float atomics.  Exactly two additions
+//     per output make the result independent of their order (FP32 addition is
+//     commutative), so the output is deterministic.
+// Warp roles and bounded waits as in tc_gemm.cuh.
+#pragma once
+
+#include <cuda.h>
+#include <cstdint>
+
+#include "ptx.cuh"
+#include "tc_gemm.cuh"
+
+namespace b200 {
+
+constexpr int SK_BM = 128;           // columns of C per tile (MMA M)
+
+template <int NP>
+struct SkTile {
+    static_assert(NP == 16 || NP == 32 || NP == 64, "padded row count");
+    static constexpr int kAStage = SK_BM * TC_ROW_BYTES;   // B^T slab: 16 KB
+    static constexpr int kBStage = NP * TC_ROW_BYTES;      // A^T rows: 2, 4 or 8 KB
+    static constexpr int kStages = NP == 64 ? 9 : 10;      // 144-160 KB of B in flight
+    static constexpr int kSmem = 1024 + kStages * (kAStage + kBStage) + TC_BAR_BYTES;
+    static constexpr uint32_t kTmemColumns = 2 * NP < 32 ? 32 : 2 * NP;
+};
+
+struct SkParams {
+    int m, n, k;
+    int num_n_tiles;          // 128-column slabs of C
+    int splits;               // 1 or 2 halves of K
+    int num_k_blocks;         // K blocks per split
+    int total_k_blocks;
+    int num_tiles;            // num_n_tiles * splits
+    float *c;
+};
+
+template <int FMT, int NP>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+tc_skinny_kernel(const __grid_constant__ CUtensorMap map_bt, const __grid_constant__ CUtensorMap map_at,
+                 const SkParams p)
+{
+    using Tile = SkTile<NP>;
+    constexpr bool kTF32 = FMT == kFmtTF32;
+    constexpr int kElem = kTF32 ? 4 : 2;
+    constexpr int kBK = TC_ROW_BYTES / kElem;
+    constexpr int kMmaK = 32 / kElem;
+    constexpr int kMmasPerStage = kBK / kMmaK;
+    constexpr bool kBtKMajor = kTF32;                      // TF32 B arrives transposed (n x k)
+    constexpr int kNB = TC_ROW_BYTES / kElem;              // columns per MN-major box (64)
+    constexpr uint32_t kBoxBytes = kBK * TC_ROW_BYTES;     // 8 KB per MN-major box
+    constexpr int kStages = Tile::kStages;
+    constexpr int kAStage = Tile::kAStage;
+    constexpr int kBStage = Tile::kBStage;
+    constexpr uint32_t kTmemColumns = Tile::kTmemColumns;
+    // Operand "A" = B^T: MN-major (FP16/BF16) or K-major (TF32); operand "B" = A^T: K-major.
+    constexpr uint32_t kIdesc = (1u << 4) | (static_cast<uint32_t>(FMT) << 7) | (static_cast<uint32_t>(FMT) << 10) |
+                                ((kBtKMajor ? 0u : 1u) << 15) | (0u << 16) |
+                                (static_cast<uint32_t>(NP >> 3) << 17) | (static_cast<uint32_t>(SK_BM >> 4) << 24);
+
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_addr(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    const uint32_t s_a = base;                              // B^T slabs
+    const uint32_t s_b = s_a + kStages * kAStage;          // A^T rows
+    const uint32_t s_bar = s_b + kStages * kBStage;
+    auto full_bar = [&](int s) { return s_bar + 8u * s; };
+    auto empty_bar = [&](int s) { return s_bar + 8u * (kStages + s); };
+    auto accf_bar = [&](int i) { return s_bar + 8u * (2 * kStages + i); };
+    auto acce_bar = [&](int i) { return s_bar + 8u * (2 * kStages + 2 + i); };
+    const uint32_t drain_bar = s_bar + 8u * (2 * kStages + 4);
+    const uint32_t tmem_slot = s_bar + 8u * (2 * kStages + 5);
+    uint32_t *tmem_slot_ptr = reinterpret_cast<uint32_t *>(smem_raw + (tmem_slot - raw));
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(accf_bar(i), 1);
+            mbar_init(acce_bar(i), 128);
+        }
+        mbar_init(drain_bar, 1);
+        fence_mbarrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_map(&map_bt);
+        tma_prefetch_map(&map_at);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, kTmemColumns);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t *>(tmem_slot_ptr);
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t filled = 0, fill_parity = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+                const int nt = tile % p.num_n_tiles;
+                const int split = tile / p.num_n_tiles;
+                const int kb0 = split * p.num_k_blocks;
+                const int kb1 = min(kb0 + p.num_k_blocks, p.total_k_blocks);
+                for (int kb = kb0; kb < kb1; ++kb) {
+                    if (!mbar_wait(empty_bar(stage), phase ^ 1u)) {
+                        report_status(kStatusLoadTimeout);
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(full_bar(stage), kAStage + kBStage);
+                    if constexpr (kBtKMajor) {
+                        tma_load_2d(s_a + stage * kAStage, &map_bt, full_bar(stage), kb * kBK, nt * SK_BM);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < SK_BM / kNB; ++j)
+                            tma_load_2d(s_a + stage * kAStage + j * kBoxBytes, &map_bt, full_bar(stage),
+                                        nt * SK_BM + j * kNB, kb * kBK);
+                    }
+                    tma_load_2d(s_b + stage * kBStage, &map_at, full_bar(stage), kb * kBK, 0);
+                    filled |= 1u << stage;
+                    fill_parity = (fill_parity & ~(1u << stage)) | (phase << stage);
+                    if (++stage == kStages) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            for (int s = 0; s < kStages; ++s)
+                if ((filled >> s) & 1u)
+                    if (!mbar_wait(full_bar(s), (fill_parity >> s) & 1u))
+                        report_status(kStatusDrainTimeout);
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            const uint64_t a_desc0 = kBtKMajor ? smem_desc_sw128(s_a, 16, 1024) : smem_desc_sw128(s_a, kBoxBytes, 1024);
+            const uint64_t b_desc0 = smem_desc_sw128(s_b, 16, 1024);
+            constexpr uint64_t kADescStage = kAStage >> 4;
+            constexpr uint64_t kBDescStage = kBStage >> 4;
+            constexpr uint64_t kADescK = kBtKMajor ? (32 >> 4) : ((kMmaK * TC_ROW_BYTES) >> 4);
+            constexpr uint64_t kBDescK = 32 >> 4;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+                const int split = tile / p.num_n_tiles;
+                const int kb0 = split * p.num_k_blocks;
+                const int kb1 = min(kb0 + p.num_k_blocks, p.total_k_blocks);
+                if (!mbar_wait(acce_bar(acc), acc_phase ^ 1u)) {
+                    report_status(kStatusMmaTimeout);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * NP);
+                for (int kb = kb0; kb < kb1; ++kb) {
+                    if (!mbar_wait(full_bar(stage), phase)) {
+                        report_status(kStatusMmaTimeout);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t a_desc = a_desc0 + static_cast<uint64_t>(stage) * kADescStage;
+                    const uint64_t b_desc = b_desc0 + static_cast<uint64_t>(stage) * kBDescStage;
+#pragma unroll
+                    for (int kk = 0; kk < kMmasPerStage; ++kk)
+                        tc_mma<kTF32>(d_tmem, a_desc + kk * kADescK, b_desc + kk * kBDescK, kIdesc,
+                                      (kb > kb0 || kk > 0) ? 1u : 0u);
+                    tc_commit(empty_bar(stage));
+                    if (++stage == kStages) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok)
+                    break;
+                tc_commit(accf_bar(acc));
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+            }
+            tc_commit(drain_bar);
+            if (!mbar_wait(drain_bar, 0))
+                report_status(kStatusDrainTimeout);
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------------------ epilogue
+        const int quarter = warp & 3;                 // TMEM lanes = columns n of C
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+            const int nt = tile % p.num_n_tiles;
+            int ok = 1;
+            if (lane == 0)
+                ok = mbar_wait(accf_bar(acc), acc_phase) ? 1 : 0;
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) {
+                if (lane == 0)
+                    report_status(kStatusEpilogueTimeout);
+                break;
+            }
+            tc_fence_after();
+            const int col = nt * SK_BM + quarter * 32 + lane;
+            const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                                   static_cast<uint32_t>(acc * NP);
+#pragma unroll 1
+            for (int chunk = 0; chunk < NP / 16; ++chunk) {
+                uint32_t v[16];
+                tmem_load_16cols(t_row + chunk * 16, v);
+                if (chunk == NP / 16 - 1) {
+                    tc_fence_before();
+                    mbar_arrive(acce_bar(acc));
+                }
+                if (col < p.n) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int row = chunk * 16 + j;
+                        if (row < p.m) {
+                            float *dst = p.c + static_cast<size_t>(row) * p.n + col;
+                            if (p.splits == 1)
+                                *dst = __uint_as_float(v[j]);
+                            else
+                                atomicAdd(dst, __uint_as_float(v[j]));
+                        }
+                    }
+                }
+            }
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1u;
+            }
+        }
+        __syncwarp();
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, kTmemColumns);
+    }
+}
+
+} // namespace b200
