@@ -75,6 +75,18 @@ int matmul_convert(void *context, int precision, const float *src, void *dst, si
 int matmul_device_status(void *context, int clear, unsigned int *status,
                          char *error, size_t error_size);
 
+/* No counterpart in the reference: the GPU form of its FP64 check
+ * (GemmReference.verify, src/precision.py:99-161).  For every output of C
+ * (m x n, FP32) computes the FP64 product of the precision-rounded inputs
+ * (TF32: round to nearest even) and the ratio |C - ref| / (5e-4 + 5e-4 |ref| +
+ * gamma_K |A||B|), gamma_K from u = 2^-23 and, for TF32, the magnitude envelope
+ * of the legal input models; writes the largest ratio to result[0] (<= 1 passes,
+ * +inf for a non-finite output) and the largest |C - ref| to result[1].
+ * Synchronises `stream`; calls that overlap on the GPU share one result slot. */
+int matmul_check_fp64(void *context, int precision, const void *a, const void *b, const float *c,
+                      int m, int k, int n, void *stream, double *result,
+                      char *error, size_t error_size);
+
 /* No counterpart in the reference.  Same arguments, result and error convention
  * as matmul_launch, for implementation 7 (tcgen05) only, but it never allocates:
  * for callers that must not call cudaMalloc or a stream-ordered allocator --

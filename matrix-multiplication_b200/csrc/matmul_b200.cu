@@ -21,6 +21,8 @@
 #include "tc_gemm.cuh"
 #include "tc2_gemm.cuh"
 #include "tc_skinny.cuh"
+#include "check.cuh"
+#include <cmath>
 
 // Scratch for matmul_launch_noalloc: a fixed array in the module's device
 // memory, so that entry point never allocates.  Every GPU that loads this
@@ -823,4 +825,56 @@ extern "C" int matmul_launch_noalloc(void *opaque, int implementation, int preci
         return fail_cuda(error, error_size, "matmul_launch_noalloc: cudaGetSymbolAddress", st);
     return launch_tcgen05(ctx, precision, a, b, c, m, k, n, static_cast<cudaStream_t>(stream), error, error_size,
                           scratch, kNoAllocScratchBytes);
+}
+
+extern "C" int matmul_check_fp64(void *opaque, int precision, const void *a, const void *b, const float *c, int m,
+                                 int k, int n, void *stream, double *result, char *error, size_t error_size)
+{
+    clear_error(error, error_size);
+    if (!opaque)
+        return fail(error, error_size, "matmul_check_fp64", "context is null");
+    if (!a || !b || !c || !result)
+        return fail(error, error_size, "matmul_check_fp64", "pointer is null");
+    if (m <= 0 || k <= 0 || n <= 0)
+        return fail(error, error_size, "matmul_check_fp64", "dimensions must be positive");
+    if (precision < 0 || precision > 3)
+        return fail(error, error_size, "matmul_check_fp64", "unknown precision");
+    Context *ctx = static_cast<Context *>(opaque);
+    cudaError_t st = cudaSetDevice(ctx->device);
+    if (st != cudaSuccess)
+        return fail_cuda(error, error_size, "cudaSetDevice", st);
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // gamma_K for u = 2^-23, as in the reference's GemmReference.
+    const double u = std::ldexp(1.0, -23);
+    const double ku = static_cast<double>(k) * u;
+    const double gamma = ku < 1.0 ? ku / (1.0 - ku) : std::expm1(static_cast<double>(k) * std::log1p(u));
+    const unsigned long long zero[2] = {0ull, 0ull};
+    st = cudaMemcpyToSymbolAsync(g_check_result, zero, sizeof(zero), 0, cudaMemcpyHostToDevice, s);
+    if (st != cudaSuccess)
+        return fail_cuda(error, error_size, "matmul_check_fp64", st);
+    const int64_t tiles = ((m + CK_TILE - 1) / CK_TILE) * static_cast<int64_t>((n + CK_TILE - 1) / CK_TILE);
+    const int grid = static_cast<int>(tiles < 8LL * ctx->sm_count ? tiles : 8LL * ctx->sm_count);
+    if (precision == kPrecFp32)
+        fp64_check_kernel<float, false><<<grid, 256, 0, s>>>(static_cast<const float *>(a),
+                                                             static_cast<const float *>(b), c, m, n, k, gamma);
+    else if (precision == kPrecTf32)
+        fp64_check_kernel<float, true><<<grid, 256, 0, s>>>(static_cast<const float *>(a),
+                                                            static_cast<const float *>(b), c, m, n, k, gamma);
+    else if (precision == kPrecBf16)
+        fp64_check_kernel<__nv_bfloat16, false><<<grid, 256, 0, s>>>(
+            static_cast<const __nv_bfloat16 *>(a), static_cast<const __nv_bfloat16 *>(b), c, m, n, k, gamma);
+    else
+        fp64_check_kernel<__half, false><<<grid, 256, 0, s>>>(static_cast<const __half *>(a),
+                                                              static_cast<const __half *>(b), c, m, n, k, gamma);
+    st = cudaGetLastError();
+    unsigned long long bits[2] = {0ull, 0ull};
+    if (st == cudaSuccess)
+        st = cudaMemcpyFromSymbolAsync(bits, g_check_result, sizeof(bits), 0, cudaMemcpyDeviceToHost, s);
+    if (st == cudaSuccess)
+        st = cudaStreamSynchronize(s);
+    if (st != cudaSuccess)
+        return fail_cuda(error, error_size, "matmul_check_fp64", st);
+    std::memcpy(&result[0], &bits[0], sizeof(double));
+    std::memcpy(&result[1], &bits[1], sizeof(double));
+    return 0;
 }

@@ -175,6 +175,24 @@ class NativeMatmul:
             raise RuntimeError(self._error_message("matmul_convert", error))
         return dst
 
+    def check_fp64(self, a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, precision: str) -> tuple[float, float]:
+        """Verify ``out`` against an FP64 product of the rounded inputs on the GPU.
+
+        Returns (largest tolerance ratio, largest absolute error); a ratio <= 1
+        passes the reference's roundoff-aware allowance.  Synchronizes.
+        """
+        if self._context is None:
+            raise RuntimeError("NativeMatmul context is closed")
+        m, k, n = validate_operands(a, b, out, precision, self._device)
+        stream = torch.cuda.current_stream(self._device)
+        result = (ctypes.c_double * 2)()
+        error = ctypes.create_string_buffer(_ERROR_SIZE)
+        if self._library.matmul_check_fp64(self._context, PRECISION_IDS[precision], ctypes.c_void_p(a.data_ptr()),
+                                           ctypes.c_void_p(b.data_ptr()), ctypes.c_void_p(out.data_ptr()), m, k, n,
+                                           ctypes.c_void_p(stream.cuda_stream), result, error, len(error)) != 0:
+            raise RuntimeError(self._error_message("matmul_check_fp64", error))
+        return float(result[0]), float(result[1])
+
     def device_status(self, clear: bool = True) -> int:
         """Synchronize and return the device status word (0 = no kernel timed out)."""
         if self._context is None:
@@ -212,6 +230,11 @@ def _bind(library) -> None:
         ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_uint), ctypes.c_char_p, ctypes.c_size_t,
     ]
     library.matmul_device_status.restype = ctypes.c_int
+    library.matmul_check_fp64.argtypes = [
+        ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
+        ctypes.c_int, ctypes.c_void_p, ctypes.POINTER(ctypes.c_double), ctypes.c_char_p, ctypes.c_size_t,
+    ]
+    library.matmul_check_fp64.restype = ctypes.c_int
 
 
 def kernel_info(library, implementation: str, precision: str) -> dict:
