@@ -384,7 +384,7 @@ int launch_tcgen05(Context *ctx, int prec, const void *a, const void *b, float *
     const bool c_direct = !(aligned16(c) && n % 4 == 0);
     if (ok && !c_direct)
         ok = encode_2d(ctx, &map_c, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, c, static_cast<uint64_t>(n),
-                       static_cast<uint64_t>(m), static_cast<uint64_t>(n) * 4, 32, 32);
+                       static_cast<uint64_t>(m), static_cast<uint64_t>(n) * 4, 32, TC_BM);
     if (!ok) {
         if (pooled)
             cudaFreeAsync(pooled, stream);

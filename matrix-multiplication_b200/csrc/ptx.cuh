@@ -135,6 +135,30 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
                  : "memory");
 }
 
+// ---------------------------------------------------------------- epilogue warpgroup
+// The four epilogue warps (128 threads) synchronise on named barrier 1; warps
+// of other roles never touch it.
+__device__ __forceinline__ void epilogue_sync()
+{
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+
+// 1 only if every epilogue thread passes 1: the four warps then take the same
+// branch, so none of them can be left waiting at barrier 1 for a warp that left.
+__device__ __forceinline__ int epilogue_all(int ok)
+{
+    uint32_t all;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.and.pred q, 1, 128, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(all)
+        : "r"(static_cast<uint32_t>(ok))
+        : "memory");
+    return static_cast<int>(all);
+}
+
 // ---------------------------------------------------------------- tcgen05
 __device__ __forceinline__ void tmem_alloc(uint32_t slot, uint32_t columns)
 {

@@ -280,7 +280,6 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     } else {
         // ------------------------------------------------------------ epilogue
         const int quarter = warp & 3;               // TMEM lanes 32*quarter .. +31
-        const uint32_t box0 = s_epi + (warp - 2) * 2 * TC_EPI_BOX;
         int acc = 0;
         uint32_t acc_phase = 0;
         uint32_t stores = 0;
@@ -290,14 +289,15 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             int ok = 1;
             if (lane == 0)
                 ok = mbar_wait(accf_bar(acc), acc_phase) ? 1 : 0;
-            ok = __shfl_sync(0xffffffffu, ok, 0);
+            ok = epilogue_all(__shfl_sync(0xffffffffu, ok, 0));
             if (!ok) {
                 if (lane == 0)
                     report_status(kStatusEpilogueTimeout);
                 break;
             }
             tc_fence_after();
-            const int row0 = mb * TC_BM + quarter * 32;
+            const int tile_row0 = mb * TC_BM;   // first row of this CTA's part of the tile
+            const int row0 = tile_row0 + quarter * 32;
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                    static_cast<uint32_t>(acc * BN);
 #pragma unroll 1
@@ -309,22 +309,26 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                     mbar_arrive(acce_bar(acc));
                 }
                 const int col0 = nb * BN + chunk * 32;
-                if (col0 >= p.n || row0 >= p.m)
+                if (col0 >= p.n || tile_row0 >= p.m)      // the same for all four warps
                     continue;
                 if (!p.c_direct) {
-                    const uint32_t box = box0 + (stores & 1u) * TC_EPI_BOX;
-                    if (lane == 0)
-                        bulk_wait_group_read<1>();
-                    __syncwarp();
-                    const uint32_t row_addr = box + lane * 128;
+                    // One 128-row x 32-column box per chunk, filled by all four warps and
+                    // stored by one thread: a quarter of the TMA operations of per-warp boxes.
+                    const uint32_t box = s_epi + (stores & 1u) * (4 * TC_EPI_BOX);
+                    const bool issuer = warp == 2 && lane == 0;
+                    if (issuer)
+                        bulk_wait_group_read<1>();        // the store that last read this buffer
+                    epilogue_sync();
+                    const int r = quarter * 32 + lane;
+                    const uint32_t row_addr = box + r * 128;
 #pragma unroll
                     for (int j = 0; j < 8; ++j)
-                        st_shared_v4(row_addr + ((j ^ (lane & 7)) << 4), v[4 * j], v[4 * j + 1], v[4 * j + 2],
+                        st_shared_v4(row_addr + ((j ^ (r & 7)) << 4), v[4 * j], v[4 * j + 1], v[4 * j + 2],
                                      v[4 * j + 3]);
                     fence_proxy_async_shared();
-                    __syncwarp();
-                    if (lane == 0) {
-                        tma_store_2d(&map_c, box, col0, row0);
+                    epilogue_sync();
+                    if (issuer) {
+                        tma_store_2d(&map_c, box, col0, tile_row0);
                         bulk_commit_group();
                     }
                     ++stores;
