@@ -23,6 +23,8 @@
 
 #include <cstdint>
 
+#include "ptx.cuh"
+
 namespace b200 {
 
 constexpr int FF_BM = 128;
@@ -38,6 +40,8 @@ ffma_gemm_kernel(const float *__restrict__ a, const float *__restrict__ b, float
     __shared__ __align__(16) float as[2][FF_BK][FF_BM];
     __shared__ __align__(16) float bs[2][FF_BK][FF_BN];
 
+    wait_for_prior_grid();
+    allow_next_grid();
     const int tid = threadIdx.x;
     const int tx = tid & 15;                 // column group
     const int ty = tid >> 4;                 // row group
@@ -237,6 +241,8 @@ ffma_gemm_async_kernel(const float *__restrict__ a, const float *__restrict__ b,
     const uint32_t as_addr = static_cast<uint32_t>(__cvta_generic_to_shared(as));
     const uint32_t bs_addr = static_cast<uint32_t>(__cvta_generic_to_shared(bs));
 
+    wait_for_prior_grid();
+    allow_next_grid();
     const int tid = threadIdx.x;
     const int tx = tid & 15;
     const int ty = tid >> 4;

@@ -136,6 +136,26 @@ cudaError_t scratch_alloc(Context *ctx, void **ptr, size_t bytes, cudaStream_t s
     return cudaMallocFromPoolAsync(ptr, bytes, ctx->pool, stream);
 }
 
+// Launch with programmatic stream serialisation: the kernel may start while the
+// previous kernel on the stream finishes; our kernels run their prologue and
+// then wait (griddepcontrol.wait) before touching global memory.
+template <typename... Params, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args &&...args)
+{
+    cudaLaunchConfig_t config{};
+    config.gridDim = grid;
+    config.blockDim = block;
+    config.dynamicSmemBytes = smem;
+    config.stream = stream;
+    cudaLaunchAttribute attribute{};
+    attribute.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attribute.val.programmaticStreamSerializationAllowed = 1;
+    config.attrs = &attribute;
+    config.numAttrs = 1;
+    return cudaLaunchKernelEx(&config, kernel, std::forward<Args>(args)...);
+}
+
 unsigned int pack_grid_x(int64_t cols)
 {
     const int64_t blocks = (cols + 255) / 256;
@@ -195,17 +215,19 @@ template <int FMT>
 cudaError_t launch_tc_kernel(int tile_n, const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &mc,
                              const TcParams &params, int grid, cudaStream_t stream)
 {
+    const dim3 block(TC_THREADS);
     if (tile_n == 0)
-        tc2_gemm_kernel<FMT><<<grid, TC_THREADS, TC2_SMEM_BYTES, stream>>>(ma, mb, mc, params);
-    else if (tile_n == 256)
-        tc_gemm_kernel<FMT, 256><<<grid, TC_THREADS, TcTile<256>::kSmem, stream>>>(ma, mb, mc, params);
-    else if (tile_n == 128)
-        tc_gemm_kernel<FMT, 128><<<grid, TC_THREADS, TcTile<128>::kSmem, stream>>>(ma, mb, mc, params);
-    else if (params.a_box_rows <= 32)
-        tc_gemm_kernel<FMT, 64, 32><<<grid, TC_THREADS, TcTile<64, 32>::kSmem, stream>>>(ma, mb, mc, params);
-    else
-        tc_gemm_kernel<FMT, 64><<<grid, TC_THREADS, TcTile<64>::kSmem, stream>>>(ma, mb, mc, params);
-    return cudaGetLastError();
+        return launch_pdl(tc2_gemm_kernel<FMT>, dim3(grid), block, TC2_SMEM_BYTES, stream, ma, mb, mc, params);
+    if (tile_n == 256)
+        return launch_pdl(tc_gemm_kernel<FMT, 256>, dim3(grid), block, TcTile<256>::kSmem, stream, ma, mb, mc,
+                          params);
+    if (tile_n == 128)
+        return launch_pdl(tc_gemm_kernel<FMT, 128>, dim3(grid), block, TcTile<128>::kSmem, stream, ma, mb, mc,
+                          params);
+    if (params.a_box_rows <= 32)
+        return launch_pdl(tc_gemm_kernel<FMT, 64, 32>, dim3(grid), block, TcTile<64, 32>::kSmem, stream, ma, mb,
+                          mc, params);
+    return launch_pdl(tc_gemm_kernel<FMT, 64>, dim3(grid), block, TcTile<64>::kSmem, stream, ma, mb, mc, params);
 }
 
 // Kernel choice: estimated time = rounds of tiles over the resident CTAs (or
@@ -240,8 +262,8 @@ template <int FMT, int NP>
 cudaError_t launch_skinny_kernel(const CUtensorMap &mbt, const CUtensorMap &mat, const SkParams &params, int grid,
                                  cudaStream_t stream)
 {
-    tc_skinny_kernel<FMT, NP><<<grid, TC_THREADS, SkTile<NP>::kSmem, stream>>>(mbt, mat, params);
-    return cudaGetLastError();
+    return launch_pdl(tc_skinny_kernel<FMT, NP>, dim3(grid), dim3(TC_THREADS), SkTile<NP>::kSmem, stream, mbt, mat,
+                      params);
 }
 
 template <int FMT>
@@ -436,7 +458,7 @@ void launch_ffma_kernel(const float *a, const float *b, float *c, int m, int k, 
     const int64_t gy = (static_cast<int64_t>(m) + FF_BM - 1) / FF_BM;
     const dim3 grid(static_cast<unsigned int>(gx < 65535 ? gx : 65535),
                     static_cast<unsigned int>(gy < 65535 ? gy : 65535));
-    ffma_gemm_kernel<VA, VB, VC><<<grid, FF_THREADS, 0, stream>>>(a, b, c, m, n, k);
+    launch_pdl(ffma_gemm_kernel<VA, VB, VC>, grid, dim3(FF_THREADS), 0, stream, a, b, c, m, n, k);
 }
 
 int launch_ffma(const float *a, const float *b, float *c, int m, int k, int n, cudaStream_t stream, char *error,
@@ -452,9 +474,10 @@ int launch_ffma(const float *a, const float *b, float *c, int m, int k, int n, c
         const dim3 grid(static_cast<unsigned int>(gx < 65535 ? gx : 65535),
                         static_cast<unsigned int>(gy < 65535 ? gy : 65535));
         if (vc)
-            ffma_gemm_async_kernel<true><<<grid, FF_THREADS, FA_SMEM_BYTES, stream>>>(a, b, c, m, n, k);
+            launch_pdl(ffma_gemm_async_kernel<true>, grid, dim3(FF_THREADS), FA_SMEM_BYTES, stream, a, b, c, m, n, k);
         else
-            ffma_gemm_async_kernel<false><<<grid, FF_THREADS, FA_SMEM_BYTES, stream>>>(a, b, c, m, n, k);
+            launch_pdl(ffma_gemm_async_kernel<false>, grid, dim3(FF_THREADS), FA_SMEM_BYTES, stream, a, b, c, m, n,
+                       k);
     } else if (va && vb && vc)
         launch_ffma_kernel<true, true, true>(a, b, c, m, k, n, stream);
     else if (va && vb)

@@ -26,6 +26,24 @@ __device__ __forceinline__ uint64_t global_timer_ns()
     return t;
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// Kernels launched with programmatic stream serialisation start while the
+// previous kernel on the stream is still finishing; each of ours runs its
+// prologue (barriers, TMEM, descriptor prefetch), then waits here for the
+// previous kernel to complete with its memory visible before touching global
+// memory.  A kernel launched without the attribute returns at once.
+__device__ __forceinline__ void wait_for_prior_grid()
+{
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// Lets the next kernel on the stream begin its own prologue on SMs this grid
+// frees; it still waits for this grid's completion before reading memory.
+__device__ __forceinline__ void allow_next_grid()
+{
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count)
 {

@@ -106,6 +106,8 @@ tc2_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
     cluster_sync_all();
     tc_fence_after();
     const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t *>(tmem_slot_ptr);
+    wait_for_prior_grid();
+    allow_next_grid();
 
     if (warp == 0) {
         // ------------------------------------------------------------ producer (both CTAs)
@@ -283,8 +285,8 @@ tc2_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
                 acc_phase ^= 1u;
             }
         }
-        if (lane == 0)
-            bulk_wait_group<0>();
+        if (warp == 2 && lane == 0)
+            bulk_wait_group_read<0>();     // shared memory free; the writes complete with the grid
         __syncwarp();
     }
 

@@ -113,6 +113,8 @@ tc_skinny_kernel(const __grid_constant__ CUtensorMap map_bt, const __grid_consta
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t *>(tmem_slot_ptr);
+    wait_for_prior_grid();
+    allow_next_grid();
 
     if (warp == 0) {
         // ------------------------------------------------------------ producer
