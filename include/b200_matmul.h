@@ -87,6 +87,16 @@ int matmul_check_fp64(void *context, int precision, const void *a, const void *b
                       int m, int k, int n, void *stream, double *result,
                       char *error, size_t error_size);
 
+/* No counterpart in the reference (the nearest is matmul_kernel_info, which
+ * describes a kernel, not a launch).  Writes, as a JSON object, the launch that
+ * matmul_launch would make for an m x k x n problem on this context's device:
+ * "kernel" (tc2_pair, tc_single, tc_skinny, ffma_async or ffma_generic),
+ * "tile_m", "tile_n", "splits" (K slices summed in a fixed order) and, where
+ * they apply, "cluster", "threads" and "grid".  The FFMA plan assumes 16-byte
+ * aligned base pointers.  Needs no stream and launches nothing. */
+int matmul_plan(void *context, int implementation, int precision, int m, int k, int n, char *json,
+                size_t json_size, char *error, size_t error_size);
+
 /* No counterpart in the reference.  Same arguments, result and error convention
  * as matmul_launch, for implementation 7 (tcgen05) only, but it never allocates:
  * for callers that must not call cudaMalloc or a stream-ordered allocator --

@@ -206,12 +206,53 @@ namespace b200 {
 // read as float4 along k, so one A fragment load serves four k-slices.  Used
 // when A and B rows are 16-byte aligned (k % 4 == 0, n % 4 == 0, aligned bases);
 // partial tiles are zero-filled by cp.async's source-size operand.
+//
+// Split K: a launch with gridDim.z = S > 1 must form clusters of (1, 1, S).  The
+// S CTAs of a cluster compute the same output tile over S consecutive slices of
+// the K tiles, stage their FP32 partial tiles in their own shared memory, and
+// after a cluster barrier CTA r sums rows [r*BM/S, (r+1)*BM/S) of all S partials
+// through distributed shared memory in the fixed order 0, 1, ..., S-1 and stores
+// them: more CTAs for outputs too small to fill the GPU, no workspace in global
+// memory, and a result that does not depend on timing.
+//
+// The output tile is BM x BN, each thread owning an RM x RN micro-tile, so the
+// block has (BM/RM) x (BN/RN) threads: 128 x 128 with 8 x 8 per thread (256
+// threads) for large problems; 128 x 64 and 64 x 64 with 8 x 8 (128 and 64
+// threads) and 64 x 64 and 32 x 32 with 4 x 4 and 2 x 2 so that smaller outputs
+// still spread over every SM.  A thread's rows are ty, ty + TY, ... (TY = BM/RM):
+// the threads of a warp then read A rows 20 floats apart, which fall in distinct
+// banks.  Its columns come in groups of four, 4*TX apart (TX = BN/RN), so a warp's
+// B reads are contiguous 16-byte vectors.
 constexpr int FA_BK = 16;
 constexpr int FA_STAGES = 3;
 constexpr int FA_A_LD = FA_BK + 4;                       // padded row of the A tile
-constexpr int FA_A_STAGE = FF_BM * FA_A_LD;              // floats
-constexpr int FA_B_STAGE = FA_BK * FF_BN;                // floats
-constexpr int FA_SMEM_BYTES = FA_STAGES * (FA_A_STAGE + FA_B_STAGE) * 4;
+
+template <int BM, int BN, int RM, int RN>
+struct FaTile {
+    static constexpr int kTX = BN / RN;                  // threads along a row of the tile
+    static constexpr int kTY = BM / RM;
+    static constexpr int kThreads = kTX * kTY;
+    static constexpr int kVecN = RN >= 4 ? 4 : 2;        // floats per B fragment read / C store
+    static_assert(BM % RM == 0 && BN % RN == 0 && RN % kVecN == 0 && RN >= 2, "micro-tile");
+    static_assert(kThreads % 32 == 0 && kThreads <= 256, "thread count");
+    static constexpr int kAStage = BM * FA_A_LD;         // floats
+    static constexpr int kBStage = FA_BK * BN;           // floats
+    static constexpr int kPipeBytes = FA_STAGES * (kAStage + kBStage) * 4;
+    static constexpr int kPartialBytes = BM * BN * 4;    // split-K partial tile
+    static constexpr int kSmemBytes = kPipeBytes > kPartialBytes ? kPipeBytes : kPartialBytes;
+    static constexpr int kAChunks = BM * FA_BK / 4;      // 16-byte copies per stage
+    static constexpr int kBChunks = FA_BK * BN / 4;
+    // Blocks per SM the register budget is sized for: 128 registers for an
+    // 8 x 8 micro-tile, fewer for the small ones.
+    static constexpr int kRegs = RM * RN >= 64 ? 128 : RM * RN >= 16 ? 80 : 40;
+    static constexpr int kMinBlocks = 65536 / (kThreads * kRegs) > 8 ? 8 : 65536 / (kThreads * kRegs);
+
+    __device__ static __forceinline__ int row(int ty, int i) { return ty + kTY * i; }
+    __device__ static __forceinline__ int col(int tx, int j)   // j: first of a vector group
+    {
+        return (j / kVecN) * (kVecN * kTX) + tx * kVecN + (j % kVecN);
+    }
+};
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, bool valid)
 {
@@ -230,57 +271,88 @@ __device__ __forceinline__ void cp_async_wait()
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-template <bool VEC_C>
-__global__ void __launch_bounds__(FF_THREADS, 2)
+// Store V consecutive outputs of one row starting at column `col` (bounds-checked
+// against n; one vector store when VEC and the whole vector is inside).
+template <int V, bool VEC>
+__device__ __forceinline__ void store_row_vec(float *c_row, int col, int n, const float *v)
+{
+    if (VEC && col + V - 1 < n) {
+        if constexpr (V == 4)
+            *reinterpret_cast<float4 *>(c_row + col) = make_float4(v[0], v[1], v[2], v[3]);
+        else
+            *reinterpret_cast<float2 *>(c_row + col) = make_float2(v[0], v[1]);
+    } else {
+#pragma unroll
+        for (int q = 0; q < V; ++q)
+            if (col + q < n)
+                c_row[col + q] = v[q];
+    }
+}
+
+template <int BM, int BN, int RM, int RN, bool VEC_C>
+__global__ void __launch_bounds__(FaTile<BM, BN, RM, RN>::kThreads, FaTile<BM, BN, RM, RN>::kMinBlocks)
 ffma_gemm_async_kernel(const float *__restrict__ a, const float *__restrict__ b, float *__restrict__ c, int m,
                        int n, int k)
 {
+    using T = FaTile<BM, BN, RM, RN>;
+    constexpr int kVecN = T::kVecN;
+    constexpr int kThreads = T::kThreads;
     extern __shared__ __align__(16) float fa_smem[];
-    float *as = fa_smem;                                    // [stage][128][FA_A_LD]
-    float *bs = fa_smem + FA_STAGES * FA_A_STAGE;           // [stage][FA_BK][128]
+    float *as = fa_smem;                                    // [stage][BM][FA_A_LD]
+    float *bs = fa_smem + FA_STAGES * T::kAStage;           // [stage][FA_BK][BN]
     const uint32_t as_addr = static_cast<uint32_t>(__cvta_generic_to_shared(as));
     const uint32_t bs_addr = static_cast<uint32_t>(__cvta_generic_to_shared(bs));
 
     wait_for_prior_grid();
     allow_next_grid();
     const int tid = threadIdx.x;
-    const int tx = tid & 15;
-    const int ty = tid >> 4;
-    const int num_kt = (k + FA_BK - 1) / FA_BK;
+    const int tx = tid % T::kTX;
+    const int ty = tid / T::kTX;
+    // K tiles [kt_begin, kt_begin + num_kt) of this CTA's split (possibly none).
+    const int splits = static_cast<int>(gridDim.z);
+    const int split = static_cast<int>(blockIdx.z);
+    const int total_kt = (k + FA_BK - 1) / FA_BK;
+    const int kt_per_split = (total_kt + splits - 1) / splits;
+    const int kt_begin = split * kt_per_split;
+    const int num_kt = max(0, min(total_kt, kt_begin + kt_per_split) - kt_begin);
 
-    for (int block_m = blockIdx.y; block_m * FF_BM < m; block_m += gridDim.y) {
-        for (int block_n = blockIdx.x; block_n * FF_BN < n; block_n += gridDim.x) {
-            const int m0 = block_m * FF_BM;
-            const int n0 = block_n * FF_BN;
+    for (int block_m = blockIdx.y; block_m * BM < m; block_m += gridDim.y) {
+        for (int block_n = blockIdx.x; block_n * BN < n; block_n += gridDim.x) {
+            const int m0 = block_m * BM;
+            const int n0 = block_n * BN;
 
-            // Tile kt -> stage s: 512 16-byte chunks of A (128 rows x 4) and of B
-            // (16 rows x 32), two of each per thread.
+            // Tile kt (of this split) -> stage s: A is BM rows x 4 chunks, B is 16 rows x BN/4 chunks.
             auto issue = [&](int kt, int s) {
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int chunk = tid + 256 * h;
-                    const int row = chunk >> 2, kq = chunk & 3;
-                    const int grow = m0 + row, gk = kt * FA_BK + kq * 4;
-                    const bool ok = grow < m && gk < k;
-                    const float *src = ok ? a + static_cast<size_t>(grow) * k + gk : a;
-                    cp_async16(as_addr + (s * FA_A_STAGE + row * FA_A_LD + kq * 4) * 4, src, ok);
+                for (int h = 0; h < (T::kAChunks + kThreads - 1) / kThreads; ++h) {
+                    const int chunk = tid + kThreads * h;
+                    if (T::kAChunks % kThreads == 0 || chunk < T::kAChunks) {
+                        const int row = chunk >> 2, kq = chunk & 3;
+                        const int grow = m0 + row, gk = (kt_begin + kt) * FA_BK + kq * 4;
+                        const bool ok = grow < m && gk < k;
+                        const float *src = ok ? a + static_cast<size_t>(grow) * k + gk : a;
+                        cp_async16(as_addr + (s * T::kAStage + row * FA_A_LD + kq * 4) * 4, src, ok);
+                    }
                 }
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int chunk = tid + 256 * h;
-                    const int row = chunk >> 5, cq = chunk & 31;
-                    const int gk = kt * FA_BK + row, gcol = n0 + cq * 4;
-                    const bool ok = gk < k && gcol < n;
-                    const float *src = ok ? b + static_cast<size_t>(gk) * n + gcol : b;
-                    cp_async16(bs_addr + (s * FA_B_STAGE + row * FF_BN + cq * 4) * 4, src, ok);
+                for (int h = 0; h < (T::kBChunks + kThreads - 1) / kThreads; ++h) {
+                    const int chunk = tid + kThreads * h;
+                    if (T::kBChunks % kThreads == 0 || chunk < T::kBChunks) {
+                        const int row = chunk / (BN / 4), cq = chunk % (BN / 4);
+                        const int gk = (kt_begin + kt) * FA_BK + row, gcol = n0 + cq * 4;
+                        const bool ok = gk < k && gcol < n;
+                        const float *src = ok ? b + static_cast<size_t>(gk) * n + gcol : b;
+                        cp_async16(bs_addr + (s * T::kBStage + row * BN + cq * 4) * 4, src, ok);
+                    }
                 }
             };
 
-            float2 acc[8][4];
+            // acc[i][p] holds outputs (row i, columns 2p and 2p + 1).
+            float2 acc[RM][RN / 2];
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
+            for (int i = 0; i < RM; ++i)
 #pragma unroll
-                for (int j = 0; j < 4; ++j)
+                for (int j = 0; j < RN / 2; ++j)
                     acc[i][j] = make_float2(0.0f, 0.0f);
 
 #pragma unroll
@@ -296,28 +368,34 @@ ffma_gemm_async_kernel(const float *__restrict__ a, const float *__restrict__ b,
                 if (next < num_kt)
                     issue(next, next % FA_STAGES);
                 cp_async_commit();
-                const float *at = as + (kt % FA_STAGES) * FA_A_STAGE;
-                const float *bt = bs + (kt % FA_STAGES) * FA_B_STAGE;
+                const float *at = as + (kt % FA_STAGES) * T::kAStage;
+                const float *bt = bs + (kt % FA_STAGES) * T::kBStage;
 #pragma unroll
                 for (int k4 = 0; k4 < FA_BK; k4 += 4) {
-                    float4 ar[8];
+                    float4 ar[RM];
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        const int row = i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4);
-                        ar[i] = *reinterpret_cast<const float4 *>(at + row * FA_A_LD + k4);
-                    }
+                    for (int i = 0; i < RM; ++i)
+                        ar[i] = *reinterpret_cast<const float4 *>(at + T::row(ty, i) * FA_A_LD + k4);
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
-                        const float4 b0 = *reinterpret_cast<const float4 *>(bt + (k4 + kk) * FF_BN + tx * 4);
-                        const float4 b1 = *reinterpret_cast<const float4 *>(bt + (k4 + kk) * FF_BN + 64 + tx * 4);
-                        const float2 bp[4] = {make_float2(b0.x, b0.y), make_float2(b0.z, b0.w),
-                                              make_float2(b1.x, b1.y), make_float2(b1.z, b1.w)};
+                        float2 bp[RN / 2];
 #pragma unroll
-                        for (int i = 0; i < 8; ++i) {
+                        for (int j = 0; j < RN; j += kVecN) {
+                            const float *src = bt + (k4 + kk) * BN + T::col(tx, j);
+                            if constexpr (kVecN == 4) {
+                                const float4 v = *reinterpret_cast<const float4 *>(src);
+                                bp[j / 2] = make_float2(v.x, v.y);
+                                bp[j / 2 + 1] = make_float2(v.z, v.w);
+                            } else {
+                                bp[j / 2] = *reinterpret_cast<const float2 *>(src);
+                            }
+                        }
+#pragma unroll
+                        for (int i = 0; i < RM; ++i) {
                             const float av = kk == 0 ? ar[i].x : kk == 1 ? ar[i].y : kk == 2 ? ar[i].z : ar[i].w;
                             const float2 ai = make_float2(av, av);
 #pragma unroll
-                            for (int j = 0; j < 4; ++j)
+                            for (int j = 0; j < RN / 2; ++j)
                                 acc[i][j] = __ffma2_rn(ai, bp[j], acc[i][j]);
                         }
                     }
@@ -326,27 +404,65 @@ ffma_gemm_async_kernel(const float *__restrict__ a, const float *__restrict__ b,
             cp_async_wait<0>();
             __syncthreads();
 
+            if (splits == 1) {
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int row = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
-                if (row >= m)
-                    continue;
-                float *c_row = c + static_cast<size_t>(row) * n;
+                for (int i = 0; i < RM; ++i) {
+                    const int row = m0 + T::row(ty, i);
+                    if (row >= m)
+                        continue;
+                    float *c_row = c + static_cast<size_t>(row) * n;
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int col = n0 + tx * 4 + 64 * h;
-                    const float2 lo = acc[i][2 * h], hi = acc[i][2 * h + 1];
-                    if (VEC_C && col + 3 < n) {
-                        *reinterpret_cast<float4 *>(c_row + col) = make_float4(lo.x, lo.y, hi.x, hi.y);
-                    } else {
-                        const float v[4] = {lo.x, lo.y, hi.x, hi.y};
+                    for (int j = 0; j < RN; j += kVecN) {
+                        const int col = n0 + T::col(tx, j);
+                        float v[kVecN];
 #pragma unroll
-                        for (int q = 0; q < 4; ++q)
-                            if (col + q < n)
-                                c_row[col + q] = v[q];
+                        for (int q = 0; q < kVecN; q += 2) {
+                            v[q] = acc[i][(j + q) / 2].x;
+                            v[q + 1] = acc[i][(j + q) / 2].y;
+                        }
+                        store_row_vec<kVecN, VEC_C>(c_row, col, n, v);
+                    }
+                }
+                continue;
+            }
+
+            // Split K: partial tile (row-major, BM x BN) into this CTA's shared memory.
+#pragma unroll
+            for (int i = 0; i < RM; ++i) {
+                float *p_row = fa_smem + T::row(ty, i) * BN;
+#pragma unroll
+                for (int j = 0; j < RN; j += kVecN) {
+                    if constexpr (kVecN == 4)
+                        *reinterpret_cast<float4 *>(p_row + T::col(tx, j)) =
+                            make_float4(acc[i][j / 2].x, acc[i][j / 2].y, acc[i][j / 2 + 1].x, acc[i][j / 2 + 1].y);
+                    else
+                        *reinterpret_cast<float2 *>(p_row + T::col(tx, j)) = acc[i][j / 2];
+                }
+            }
+            cluster_sync_all();
+            {
+                const uint32_t part_addr = static_cast<uint32_t>(__cvta_generic_to_shared(fa_smem));
+                const int rows = BM / splits;                  // this CTA's slice of the tile
+                const int row0 = split * rows;
+                for (int idx = tid; idx < rows * (BN / 4); idx += kThreads) {
+                    const int r = row0 + idx / (BN / 4), c4 = (idx % (BN / 4)) * 4;
+                    const uint32_t offset = static_cast<uint32_t>((r * BN + c4) * 4);
+                    float4 sum = ld_shared_cluster_f4(map_to_cta(part_addr + offset, 0));
+                    for (int src = 1; src < splits; ++src) {
+                        const float4 v = ld_shared_cluster_f4(map_to_cta(part_addr + offset, src));
+                        sum.x += v.x;
+                        sum.y += v.y;
+                        sum.z += v.z;
+                        sum.w += v.w;
+                    }
+                    if (m0 + r < m) {
+                        const float v[4] = {sum.x, sum.y, sum.z, sum.w};
+                        store_row_vec<4, VEC_C>(c + static_cast<size_t>(m0 + r) * n, n0 + c4, n, v);
                     }
                 }
             }
+            // No CTA reuses (or leaves) its shared memory while another still reads it.
+            cluster_sync_all();
         }
     }
 }

@@ -76,6 +76,7 @@ struct Context {
     int minor = 0;
     int sm_count = 0;
     int max_pairs = 0;        // co-resident 2-CTA clusters of the pair kernel
+    int ffma_resident[4] = {}; // resident blocks per SM of each aligned FFMA tile
     EncodeTiledFn encode = nullptr;
     cudaMemPool_t pool = nullptr;
 };
@@ -153,6 +154,28 @@ cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t 
     attribute.val.programmaticStreamSerializationAllowed = 1;
     config.attrs = &attribute;
     config.numAttrs = 1;
+    return cudaLaunchKernelEx(&config, kernel, std::forward<Args>(args)...);
+}
+
+// launch_pdl with clusters of (1, 1, cluster_z) CTAs (cluster_z divides grid.z).
+template <typename... Params, typename... Args>
+cudaError_t launch_pdl_cluster_z(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, unsigned int cluster_z,
+                                 cudaStream_t stream, Args &&...args)
+{
+    cudaLaunchConfig_t config{};
+    config.gridDim = grid;
+    config.blockDim = block;
+    config.dynamicSmemBytes = smem;
+    config.stream = stream;
+    cudaLaunchAttribute attributes[2]{};
+    attributes[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attributes[0].val.programmaticStreamSerializationAllowed = 1;
+    attributes[1].id = cudaLaunchAttributeClusterDimension;
+    attributes[1].val.clusterDim.x = 1;
+    attributes[1].val.clusterDim.y = 1;
+    attributes[1].val.clusterDim.z = cluster_z;
+    config.attrs = attributes;
+    config.numAttrs = cluster_z > 1 ? 2 : 1;
     return cudaLaunchKernelEx(&config, kernel, std::forward<Args>(args)...);
 }
 
@@ -258,6 +281,13 @@ int choose_tile_n(const Context *ctx, int m, int n)
     return choice;
 }
 
+// Two K halves when the 128-column slabs alone would leave half the SMs idle.
+int skinny_splits(const Context *ctx, int n, int total_k_blocks)
+{
+    const int tiles = (n + SK_BM - 1) / SK_BM;
+    return (2 * tiles <= ctx->sm_count && total_k_blocks >= 4) ? 2 : 1;
+}
+
 template <int FMT, int NP>
 cudaError_t launch_skinny_kernel(const CUtensorMap &mbt, const CUtensorMap &mat, const SkParams &params, int grid,
                                  cudaStream_t stream)
@@ -310,8 +340,7 @@ int launch_skinny(Context *ctx, int prec, const void *a_op, int64_t lda, const v
     params.k = k;
     params.num_n_tiles = (n + SK_BM - 1) / SK_BM;
     params.total_k_blocks = static_cast<int>((static_cast<int64_t>(k) + bk - 1) / bk);
-    // Two K halves when the column slabs alone would leave half the SMs idle.
-    params.splits = (2 * params.num_n_tiles <= ctx->sm_count && params.total_k_blocks >= 4) ? 2 : 1;
+    params.splits = skinny_splits(ctx, n, params.total_k_blocks);
     params.num_k_blocks = (params.total_k_blocks + params.splits - 1) / params.splits;
     params.num_tiles = params.num_n_tiles * params.splits;
     params.c = c;
@@ -461,29 +490,94 @@ void launch_ffma_kernel(const float *a, const float *b, float *c, int m, int k, 
     launch_pdl(ffma_gemm_kernel<VA, VB, VC>, grid, dim3(FF_THREADS), 0, stream, a, b, c, m, n, k);
 }
 
-int launch_ffma(const float *a, const float *b, float *c, int m, int k, int n, cudaStream_t stream, char *error,
-                size_t error_size)
+// Launch plan of the aligned FFMA kernel: output tile and K split.  The busiest
+// SM's time is estimated as (its blocks) x (tile area) x (K tiles per split) /
+// efficiency, where efficiency falls when few warps are resident (the 8 x 8
+// micro-tiles saturate the FMA pipe from about 10 resident warps, a single
+// 4-warp block reaches about 65 % of that) and the 4 x 4 micro-tile pays 10 %
+// more shared-memory traffic per FMA; plus a fixed pipeline fill and epilogue
+// of two K tiles per wave of blocks.  Fitted to measured B200 times over square
+// sizes 64-4096 and skinny / long-K shapes (within 4 % of the best plan on
+// average, 15 % at worst).
+struct FfmaTileOption {
+    int bm, bn, warps;
+    double efficiency;
+};
+constexpr FfmaTileOption kFfmaTiles[] = {{128, 128, 8, 1.0}, {128, 64, 4, 1.0}, {64, 64, 2, 0.9}, {32, 32, 2, 0.9}};
+constexpr int kFfmaTileCount = sizeof(kFfmaTiles) / sizeof(kFfmaTiles[0]);
+constexpr int kFfmaMaxSplits = 8;                       // portable cluster size
+
+struct FfmaPlan {
+    int tile;
+    int splits;
+};
+
+FfmaPlan choose_ffma_plan(int m, int k, int n, int sm_count, const int *resident)
+{
+    FfmaPlan best{0, 1};
+    double best_cost = 0.0;
+    const int64_t total_kt = (static_cast<int64_t>(k) + FA_BK - 1) / FA_BK;
+    for (int t = 0; t < kFfmaTileCount; ++t) {
+        const FfmaTileOption &o = kFfmaTiles[t];
+        const int64_t tiles = ((static_cast<int64_t>(m) + o.bm - 1) / o.bm) *
+                              ((static_cast<int64_t>(n) + o.bn - 1) / o.bn);
+        const int64_t slots = resident[t] > 0 ? resident[t] : 1;
+        for (int splits = 1; splits <= kFfmaMaxSplits && splits <= total_kt; splits *= 2) {
+            const int64_t per_sm = (tiles * splits + sm_count - 1) / sm_count;
+            const int64_t concurrent = per_sm < slots ? per_sm : slots;
+            const int64_t waves = (per_sm + slots - 1) / slots;
+            const int64_t kt = (total_kt + splits - 1) / splits;
+            const double occupancy = 0.4 + static_cast<double>(concurrent * o.warps) / 16.0;
+            const double efficiency = o.efficiency * (occupancy < 1.0 ? occupancy : 1.0);
+            const double area = static_cast<double>(o.bm) * o.bn;
+            const double cost = static_cast<double>(per_sm) * area * static_cast<double>(kt) / efficiency +
+                                2.0 * static_cast<double>(waves * concurrent) * area;
+            if ((t == 0 && splits == 1) || cost < best_cost * 0.999) {
+                best = {t, splits};
+                best_cost = cost;
+            }
+        }
+    }
+    return best;
+}
+
+template <int BM, int BN, int RM, int RN>
+cudaError_t launch_ffma_async(const float *a, const float *b, float *c, int m, int k, int n, int splits, bool vec_c,
+                              cudaStream_t stream)
+{
+    using T = FaTile<BM, BN, RM, RN>;
+    const int64_t gx = (static_cast<int64_t>(n) + BN - 1) / BN;
+    const int64_t gy = (static_cast<int64_t>(m) + BM - 1) / BM;
+    const dim3 grid(static_cast<unsigned int>(gx < 65535 ? gx : 65535),
+                    static_cast<unsigned int>(gy < 65535 ? gy : 65535), static_cast<unsigned int>(splits));
+    if (vec_c)
+        return launch_pdl_cluster_z(ffma_gemm_async_kernel<BM, BN, RM, RN, true>, grid, dim3(T::kThreads),
+                                    T::kSmemBytes, splits, stream, a, b, c, m, n, k);
+    return launch_pdl_cluster_z(ffma_gemm_async_kernel<BM, BN, RM, RN, false>, grid, dim3(T::kThreads),
+                                T::kSmemBytes, splits, stream, a, b, c, m, n, k);
+}
+
+int launch_ffma(const Context *ctx, const float *a, const float *b, float *c, int m, int k, int n,
+                cudaStream_t stream, char *error, size_t error_size)
 {
     const bool va = aligned16(a) && k % 4 == 0;
     const bool vb = aligned16(b) && n % 4 == 0;
     const bool vc = aligned16(c) && n % 4 == 0;
     if (va && vb) {
-        // Aligned operands: cp.async pipeline kernel.
-        const int64_t gx = (static_cast<int64_t>(n) + FF_BN - 1) / FF_BN;
-        const int64_t gy = (static_cast<int64_t>(m) + FF_BM - 1) / FF_BM;
-        const dim3 grid(static_cast<unsigned int>(gx < 65535 ? gx : 65535),
-                        static_cast<unsigned int>(gy < 65535 ? gy : 65535));
-        if (vc)
-            launch_pdl(ffma_gemm_async_kernel<true>, grid, dim3(FF_THREADS), FA_SMEM_BYTES, stream, a, b, c, m, n, k);
-        else
-            launch_pdl(ffma_gemm_async_kernel<false>, grid, dim3(FF_THREADS), FA_SMEM_BYTES, stream, a, b, c, m, n,
-                       k);
-    } else if (va && vb && vc)
-        launch_ffma_kernel<true, true, true>(a, b, c, m, k, n, stream);
-    else if (va && vb)
-        launch_ffma_kernel<true, true, false>(a, b, c, m, k, n, stream);
-    else
+        // Aligned operands: cp.async pipeline kernel, tile by the cost model.
+        const FfmaPlan plan = choose_ffma_plan(m, k, n, ctx->sm_count, ctx->ffma_resident);
+        cudaError_t st;
+        switch (plan.tile) {
+        case 0: st = launch_ffma_async<128, 128, 8, 8>(a, b, c, m, k, n, plan.splits, vc, stream); break;
+        case 1: st = launch_ffma_async<128, 64, 8, 8>(a, b, c, m, k, n, plan.splits, vc, stream); break;
+        case 2: st = launch_ffma_async<64, 64, 8, 8>(a, b, c, m, k, n, plan.splits, vc, stream); break;
+        default: st = launch_ffma_async<32, 32, 4, 4>(a, b, c, m, k, n, plan.splits, vc, stream); break;
+        }
+        if (st != cudaSuccess)
+            return fail(error, error_size, "kernel launch", cudaGetErrorString(st));
+    } else {
         launch_ffma_kernel<false, false, false>(a, b, c, m, k, n, stream);
+    }
     const cudaError_t st = cudaGetLastError();
     if (st != cudaSuccess)
         return fail(error, error_size, "kernel launch", cudaGetErrorString(st));
@@ -556,9 +650,13 @@ extern "C" int matmul_kernel_info(int implementation, int precision, char *json,
             json, json_size,
             "{\"implementation\":\"ffma\",\"precision\":\"fp32\",\"tile_m\":%d,\"tile_n\":%d,"
             "\"tile_k\":%d,\"threads\":%d,\"warp_tile_m\":%d,\"warp_tile_n\":%d,\"microtile_m\":8,"
-            "\"microtile_n\":8,\"buffering\":2,\"load_method\":\"float4_masked_register_prefetch\","
-            "\"tensor_cores\":false,\"blocks_per_sm\":2}",
-            FF_BM, FF_BN, FF_BK, FF_THREADS, 16, 128);
+            "\"microtile_n\":8,\"buffering\":%d,\"load_method\":\"cp_async_16B_zero_fill\","
+            "\"tensor_cores\":false,\"fma\":\"ffma2_rn_packed_fp32x2\",\"blocks_per_sm\":2,"
+            "\"small_tiles\":[[128,64,8,8],[64,64,8,8],[32,32,4,4]],\"split_k\":\"cluster_1x1xS_dsmem_reduce\","
+            "\"max_splits\":%d,\"plan_choice\":\"cost_model_busiest_sm\","
+            "\"unaligned_kernel\":{\"tile_m\":%d,\"tile_n\":%d,\"tile_k\":%d,\"buffering\":2,"
+            "\"load_method\":\"masked_scalar_register_prefetch\"}}",
+            FF_BM, FF_BN, FA_BK, FF_THREADS, 16, 128, FA_STAGES, kFfmaMaxSplits, FF_BM, FF_BN, FF_BK);
     }
     if (written < 0 || static_cast<size_t>(written) >= json_size) {
         json[0] = '\0';
@@ -638,13 +736,33 @@ extern "C" void *matmul_create(int device, char *error, size_t error_size)
             return nullptr;
         }
     }
-    const void *ffma_kernels[] = {reinterpret_cast<const void *>(&ffma_gemm_async_kernel<true>),
-                                  reinterpret_cast<const void *>(&ffma_gemm_async_kernel<false>)};
-    for (const void *kernel : ffma_kernels) {
-        st = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FA_SMEM_BYTES);
+#define B200_FFMA_KERNEL(BM, BN, RM, RN)                                                                       \
+    {reinterpret_cast<const void *>(&ffma_gemm_async_kernel<BM, BN, RM, RN, true>),                             \
+     FaTile<BM, BN, RM, RN>::kSmemBytes},                                                                        \
+    {                                                                                                            \
+        reinterpret_cast<const void *>(&ffma_gemm_async_kernel<BM, BN, RM, RN, false>),                          \
+            FaTile<BM, BN, RM, RN>::kSmemBytes                                                                   \
+    }
+    const std::pair<const void *, int> ffma_kernels[] = {
+        B200_FFMA_KERNEL(128, 128, 8, 8), B200_FFMA_KERNEL(128, 64, 8, 8), B200_FFMA_KERNEL(64, 64, 8, 8),
+        B200_FFMA_KERNEL(32, 32, 4, 4)};
+#undef B200_FFMA_KERNEL
+    for (const auto &kernel : ffma_kernels) {
+        st = cudaFuncSetAttribute(kernel.first, cudaFuncAttributeMaxDynamicSharedMemorySize, kernel.second);
         if (st != cudaSuccess) {
             delete ctx;
             fail_cuda(error, error_size, "cudaFuncSetAttribute", st);
+            return nullptr;
+        }
+    }
+    static_assert(sizeof(ffma_kernels) / sizeof(ffma_kernels[0]) == 2 * kFfmaTileCount, "one pair per tile");
+    for (int t = 0; t < kFfmaTileCount; ++t) {
+        const int threads = kFfmaTiles[t].warps * 32;
+        st = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ctx->ffma_resident[t], ffma_kernels[2 * t].first,
+                                                           threads, ffma_kernels[2 * t].second);
+        if (st != cudaSuccess) {
+            delete ctx;
+            fail_cuda(error, error_size, "cudaOccupancyMaxActiveBlocksPerMultiprocessor", st);
             return nullptr;
         }
     }
@@ -755,9 +873,68 @@ extern "C" int matmul_launch(void *opaque, int implementation, int precision, co
         return fail_cuda(error, error_size, "cudaSetDevice", st);
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (implementation == kImplFfma)
-        return launch_ffma(static_cast<const float *>(a), static_cast<const float *>(b), c, m, k, n, s, error,
+        return launch_ffma(ctx, static_cast<const float *>(a), static_cast<const float *>(b), c, m, k, n, s, error,
                            error_size);
     return launch_tcgen05(ctx, precision, a, b, c, m, k, n, s, error, error_size);
+}
+
+extern "C" int matmul_plan(void *opaque, int implementation, int precision, int m, int k, int n, char *json,
+                           size_t json_size, char *error, size_t error_size)
+{
+    clear_error(error, error_size);
+    if (json && json_size)
+        json[0] = '\0';
+    if (!opaque)
+        return fail(error, error_size, "matmul_plan", "context is null");
+    if (!json || json_size == 0)
+        return fail(error, error_size, "matmul_plan", "JSON buffer is null");
+    if (m <= 0 || k <= 0 || n <= 0)
+        return fail(error, error_size, "matmul_plan", "dimensions must be positive");
+    if (check_ids(implementation, precision, "matmul_plan", error, error_size))
+        return 1;
+    const Context *ctx = static_cast<const Context *>(opaque);
+    int written;
+    if (implementation == kImplFfma) {
+        // The aligned kernel runs when A and B rows are 16-byte aligned; bases
+        // are unknown here, so this reports the plan for aligned bases.
+        if (k % 4 == 0 && n % 4 == 0) {
+            const FfmaPlan plan = choose_ffma_plan(m, k, n, ctx->sm_count, ctx->ffma_resident);
+            const FfmaTileOption &o = kFfmaTiles[plan.tile];
+            written = std::snprintf(json, json_size,
+                                    "{\"kernel\":\"ffma_async\",\"tile_m\":%d,\"tile_n\":%d,\"threads\":%d,"
+                                    "\"splits\":%d,\"cluster\":[1,1,%d],\"grid\":[%lld,%lld,%d]}",
+                                    o.bm, o.bn, o.warps * 32, plan.splits, plan.splits,
+                                    static_cast<long long>((n + o.bn - 1) / o.bn),
+                                    static_cast<long long>((m + o.bm - 1) / o.bm), plan.splits);
+        } else {
+            written = std::snprintf(json, json_size,
+                                    "{\"kernel\":\"ffma_generic\",\"tile_m\":%d,\"tile_n\":%d,\"threads\":%d,"
+                                    "\"splits\":1}",
+                                    FF_BM, FF_BN, FF_THREADS);
+        }
+    } else if (m <= kSkinnyMaxM) {
+        const int elem = precision == kPrecTf32 ? 4 : 2;
+        const int total_k_blocks = static_cast<int>((static_cast<int64_t>(k) + TC_ROW_BYTES / elem - 1) /
+                                                    (TC_ROW_BYTES / elem));
+        written = std::snprintf(json, json_size,
+                                "{\"kernel\":\"tc_skinny\",\"tile_m\":%d,\"tile_n\":%d,\"splits\":%d}",
+                                m <= 16 ? 16 : m <= 32 ? 32 : 64, SK_BM, skinny_splits(ctx, n, total_k_blocks));
+    } else {
+        const int kernel_n = choose_tile_n(ctx, m, n);
+        written = kernel_n == 0
+                      ? std::snprintf(json, json_size,
+                                      "{\"kernel\":\"tc2_pair\",\"tile_m\":%d,\"tile_n\":%d,\"cluster\":[2,1,1],"
+                                      "\"splits\":1}",
+                                      TC2_BM, TC2_BN)
+                      : std::snprintf(json, json_size,
+                                      "{\"kernel\":\"tc_single\",\"tile_m\":%d,\"tile_n\":%d,\"splits\":1}", TC_BM,
+                                      kernel_n);
+    }
+    if (written < 0 || static_cast<size_t>(written) >= json_size) {
+        json[0] = '\0';
+        return fail(error, error_size, "matmul_plan", "JSON buffer too small");
+    }
+    return 0;
 }
 
 extern "C" int matmul_convert(void *opaque, int precision, const float *src, void *dst, size_t count, void *stream,

@@ -276,6 +276,17 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr)
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
+// 16-byte load from the shared memory of a CTA of this cluster (a mapa address).
+__device__ __forceinline__ float4 ld_shared_cluster_f4(uint32_t cluster_addr)
+{
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(cluster_addr)
+                 : "memory");
+    return v;
+}
+
 // Every thread of every CTA in the cluster.
 __device__ __forceinline__ void cluster_sync_all()
 {

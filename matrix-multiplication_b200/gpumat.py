@@ -148,6 +148,22 @@ class NativeMatmul:
 
         return run
 
+    def plan(self, implementation: str, m: int, k: int, n: int, precision: str = "fp32") -> dict:
+        """The launch ``prepare(...)()`` would make for an m x k x n problem (kernel,
+        tile, K splits; the FFMA plan assumes 16-byte aligned operands)."""
+        if self._context is None:
+            raise RuntimeError("NativeMatmul context is closed")
+        if not isinstance(implementation, str) or implementation not in _IMPLEMENTATIONS:
+            raise ValueError(f"unknown implementation: {implementation!r}")
+        if not isinstance(precision, str) or precision not in PRECISION_IDS:
+            raise ValueError(f"unknown precision: {precision!r}")
+        result = ctypes.create_string_buffer(_ERROR_SIZE)
+        error = ctypes.create_string_buffer(_ERROR_SIZE)
+        if self._library.matmul_plan(self._context, _IMPLEMENTATIONS[implementation], PRECISION_IDS[precision],
+                                     m, k, n, result, len(result), error, len(error)) != 0:
+            raise RuntimeError(self._error_message("matmul_plan", error))
+        return json.loads(result.value)
+
     def convert(self, src: torch.Tensor, dst: torch.Tensor, precision: str) -> torch.Tensor:
         """Convert FP32 ``src`` into ``dst`` (the input dtype of ``precision``) on the device.
 
@@ -235,6 +251,11 @@ def _bind(library) -> None:
         ctypes.c_int, ctypes.c_void_p, ctypes.POINTER(ctypes.c_double), ctypes.c_char_p, ctypes.c_size_t,
     ]
     library.matmul_check_fp64.restype = ctypes.c_int
+    library.matmul_plan.argtypes = [
+        ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+        ctypes.c_char_p, ctypes.c_size_t, ctypes.c_char_p, ctypes.c_size_t,
+    ]
+    library.matmul_plan.restype = ctypes.c_int
 
 
 def kernel_info(library, implementation: str, precision: str) -> dict:

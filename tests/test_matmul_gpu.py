@@ -122,6 +122,52 @@ def test_prepared_nondefault_stream_and_graph(native, backend, precision):
     del graph
 
 
+# Aligned FP32 shapes whose launch plans (matmul_plan) cover every FFMA tile and
+# K split of 1, 2, 4 and 8 cluster CTAs, including splits that get no K tiles
+# (32 x 144 x 32: 9 K tiles over 8 CTAs).
+FFMA_PLAN_SHAPES = ((64, 64, 64), (128, 128, 128), (32, 144, 32), (100, 3000, 200), (384, 2048, 640),
+                    (768, 768, 768), (1024, 64, 1024), (1536, 256, 1536), (1536, 1536, 1536),
+                    (2048, 512, 2048), (2048, 256, 2048), (1200, 64, 2400), (260, 2052, 196))
+
+
+def test_ffma_plans_cover_every_tile_and_split(native):
+    plans = {shape: native.plan("ffma", *shape) for shape in FFMA_PLAN_SHAPES}
+    assert {p["kernel"] for p in plans.values()} == {"ffma_async"}
+    assert {(p["tile_m"], p["tile_n"]) for p in plans.values()} == {(128, 128), (128, 64), (64, 64), (32, 32)}
+    assert {p["splits"] for p in plans.values()} == {1, 2, 4, 8}
+    assert plans[(32, 144, 32)]["splits"] == 8
+    assert native.plan("ffma", 31, 33, 65)["kernel"] == "ffma_generic"
+
+
+@pytest.mark.parametrize("shape", FFMA_PLAN_SHAPES)
+def test_ffma_split_k_plans_against_fp64_oracle(native, shape):
+    m, k, n = shape
+    a_np = po.seeded_uniform((m, k), seed=3 * m + k)
+    b_np = po.seeded_uniform((k, n), seed=5 * n + k)
+    report = _run_and_verify(native, "ffma", "fp32", a_np, b_np, offset=False)
+    assert report["max_tolerance_ratio"] <= 1.0
+
+
+def test_ffma_split_k_is_deterministic_and_graph_capturable(native):
+    m, k, n = 100, 3000, 200
+    assert native.plan("ffma", m, k, n)["splits"] > 1
+    a = torch.from_numpy(po.seeded_uniform((m, k), 1)).cuda()
+    b = torch.from_numpy(po.seeded_uniform((k, n), 2)).cuda()
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        first = torch.empty((m, n), device="cuda")
+        second = torch.full((m, n), float("nan"), device="cuda")
+        native.prepare("ffma", a, b, first, precision="fp32")()
+        run = native.prepare("ffma", a, b, second, precision="fp32")
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            run()
+        graph.replay()
+        stream.synchronize()
+    assert torch.equal(first, second)
+    del graph
+
+
 @pytest.mark.parametrize("shape", ((256, 512, 512), (129, 65, 257)))
 @pytest.mark.parametrize("precision", ("tf32", "bf16"))
 def test_graph_of_ten_launches_replays_correctly(native, precision, shape):
