@@ -200,11 +200,11 @@ ffma_gemm_kernel(const float *__restrict__ a, const float *__restrict__ b, float
 namespace b200 {
 
 // ---------------------------------------------------------------------------
-// Aligned-operand variant: a 3-stage cp.async pipeline feeds shared memory
-// straight from global memory (no register staging, one barrier per 16-deep K
-// tile).  A stays row-major in shared memory (rows padded to 20 floats) and is
-// read as float4 along k, so one A fragment load serves four k-slices.  Used
-// when A and B rows are 16-byte aligned (k % 4 == 0, n % 4 == 0, aligned bases);
+// Aligned-operand variant: a 3- or 4-stage cp.async pipeline feeds shared memory
+// straight from global memory (no register staging, one barrier per 16- or
+// 32-deep K tile).  A stays row-major in shared memory (rows padded by 4 floats)
+// and is read as float4 along k, so one A fragment load serves four k-slices.
+// Used when A and B rows are 16-byte aligned (k % 4 == 0, n % 4 == 0, aligned bases);
 // partial tiles are zero-filled by cp.async's source-size operand.
 //
 // Split K: a launch with gridDim.z = S > 1 must form clusters of (1, 1, S).  The
@@ -217,15 +217,12 @@ namespace b200 {
 //
 // The output tile is BM x BN, each thread owning an RM x RN micro-tile, so the
 // block has (BM/RM) x (BN/RN) threads: 128 x 128 with 8 x 8 per thread (256
-// threads) for large problems; 128 x 64 and 64 x 64 with 8 x 8 (128 and 64
-// threads) and 64 x 64 and 32 x 32 with 4 x 4 and 2 x 2 so that smaller outputs
-// still spread over every SM.  A thread's rows are ty, ty + TY, ... (TY = BM/RM):
-// the threads of a warp then read A rows 20 floats apart, which fall in distinct
+// threads) for large problems and 32 x 32 with 4 x 4 (64 threads) so that
+// smaller outputs still spread over every SM.  A thread's rows are ty, ty + TY, ... (TY = BM/RM): the
+// threads of a warp then read A rows BK + 4 floats apart, which fall in distinct
 // banks.  Its columns come in groups of four, 4*TX apart (TX = BN/RN), so a warp's
 // B reads are contiguous 16-byte vectors.
-constexpr int FA_BK = 16;
-constexpr int FA_STAGES = 3;
-constexpr int FA_A_LD = FA_BK + 4;                       // padded row of the A tile
+constexpr int FA_MODEL_BK = 16;                          // K granularity of the launch-plan model
 
 template <int BM, int BN, int RM, int RN>
 struct FaTile {
@@ -235,13 +232,19 @@ struct FaTile {
     static constexpr int kVecN = RN >= 4 ? 4 : 2;        // floats per B fragment read / C store
     static_assert(BM % RM == 0 && BN % RN == 0 && RN % kVecN == 0 && RN >= 2, "micro-tile");
     static_assert(kThreads % 32 == 0 && kThreads <= 256, "thread count");
-    static constexpr int kAStage = BM * FA_A_LD;         // floats
-    static constexpr int kBStage = FA_BK * BN;           // floats
-    static constexpr int kPipeBytes = FA_STAGES * (kAStage + kBStage) * 4;
+    // K depth and ring length per tile: the 128 x 128 tile takes 32-deep stages
+    // (half the barriers per FMA; two blocks still fit an SM), smaller tiles
+    // 16-deep ones (four stages from 64 x 64 up, three below).
+    static constexpr int kBK = BM * BN >= 128 * 128 ? 32 : 16;
+    static constexpr int kStages = BM * BN >= 128 * 128 ? 3 : BM * BN >= 64 * 64 ? 4 : 3;
+    static constexpr int kALd = kBK + 4;                 // padded row of the A tile (floats)
+    static constexpr int kAStage = BM * kALd;            // floats
+    static constexpr int kBStage = kBK * BN;             // floats
+    static constexpr int kPipeBytes = kStages * (kAStage + kBStage) * 4;
     static constexpr int kPartialBytes = BM * BN * 4;    // split-K partial tile
     static constexpr int kSmemBytes = kPipeBytes > kPartialBytes ? kPipeBytes : kPartialBytes;
-    static constexpr int kAChunks = BM * FA_BK / 4;      // 16-byte copies per stage
-    static constexpr int kBChunks = FA_BK * BN / 4;
+    static constexpr int kAChunks = BM * kBK / 4;        // 16-byte copies per stage
+    static constexpr int kBChunks = kBK * BN / 4;
     // Blocks per SM the register budget is sized for: 128 registers for an
     // 8 x 8 micro-tile, fewer for the small ones.
     static constexpr int kRegs = RM * RN >= 64 ? 128 : RM * RN >= 16 ? 80 : 40;
@@ -295,11 +298,12 @@ ffma_gemm_async_kernel(const float *__restrict__ a, const float *__restrict__ b,
                        int n, int k)
 {
     using T = FaTile<BM, BN, RM, RN>;
+    constexpr int BK = T::kBK, STAGES = T::kStages, A_LD = T::kALd;
     constexpr int kVecN = T::kVecN;
     constexpr int kThreads = T::kThreads;
     extern __shared__ __align__(16) float fa_smem[];
-    float *as = fa_smem;                                    // [stage][BM][FA_A_LD]
-    float *bs = fa_smem + FA_STAGES * T::kAStage;           // [stage][FA_BK][BN]
+    float *as = fa_smem;                                    // [stage][BM][A_LD]
+    float *bs = fa_smem + STAGES * T::kAStage;           // [stage][BK][BN]
     const uint32_t as_addr = static_cast<uint32_t>(__cvta_generic_to_shared(as));
     const uint32_t bs_addr = static_cast<uint32_t>(__cvta_generic_to_shared(bs));
 
@@ -311,7 +315,7 @@ ffma_gemm_async_kernel(const float *__restrict__ a, const float *__restrict__ b,
     // K tiles [kt_begin, kt_begin + num_kt) of this CTA's split (possibly none).
     const int splits = static_cast<int>(gridDim.z);
     const int split = static_cast<int>(blockIdx.z);
-    const int total_kt = (k + FA_BK - 1) / FA_BK;
+    const int total_kt = (k + BK - 1) / BK;
     const int kt_per_split = (total_kt + splits - 1) / splits;
     const int kt_begin = split * kt_per_split;
     const int num_kt = max(0, min(total_kt, kt_begin + kt_per_split) - kt_begin);
@@ -321,17 +325,17 @@ ffma_gemm_async_kernel(const float *__restrict__ a, const float *__restrict__ b,
             const int m0 = block_m * BM;
             const int n0 = block_n * BN;
 
-            // Tile kt (of this split) -> stage s: A is BM rows x 4 chunks, B is 16 rows x BN/4 chunks.
+            // Tile kt (of this split) -> stage s: A is BM rows x BK/4 chunks, B is BK rows x BN/4 chunks.
             auto issue = [&](int kt, int s) {
 #pragma unroll
                 for (int h = 0; h < (T::kAChunks + kThreads - 1) / kThreads; ++h) {
                     const int chunk = tid + kThreads * h;
                     if (T::kAChunks % kThreads == 0 || chunk < T::kAChunks) {
-                        const int row = chunk >> 2, kq = chunk & 3;
-                        const int grow = m0 + row, gk = (kt_begin + kt) * FA_BK + kq * 4;
+                        const int row = chunk / (BK / 4), kq = chunk % (BK / 4);
+                        const int grow = m0 + row, gk = (kt_begin + kt) * BK + kq * 4;
                         const bool ok = grow < m && gk < k;
                         const float *src = ok ? a + static_cast<size_t>(grow) * k + gk : a;
-                        cp_async16(as_addr + (s * T::kAStage + row * FA_A_LD + kq * 4) * 4, src, ok);
+                        cp_async16(as_addr + (s * T::kAStage + row * A_LD + kq * 4) * 4, src, ok);
                     }
                 }
 #pragma unroll
@@ -339,7 +343,7 @@ ffma_gemm_async_kernel(const float *__restrict__ a, const float *__restrict__ b,
                     const int chunk = tid + kThreads * h;
                     if (T::kBChunks % kThreads == 0 || chunk < T::kBChunks) {
                         const int row = chunk / (BN / 4), cq = chunk % (BN / 4);
-                        const int gk = (kt_begin + kt) * FA_BK + row, gcol = n0 + cq * 4;
+                        const int gk = (kt_begin + kt) * BK + row, gcol = n0 + cq * 4;
                         const bool ok = gk < k && gcol < n;
                         const float *src = ok ? b + static_cast<size_t>(gk) * n + gcol : b;
                         cp_async16(bs_addr + (s * T::kBStage + row * BN + cq * 4) * 4, src, ok);
@@ -356,26 +360,26 @@ ffma_gemm_async_kernel(const float *__restrict__ a, const float *__restrict__ b,
                     acc[i][j] = make_float2(0.0f, 0.0f);
 
 #pragma unroll
-            for (int s = 0; s < FA_STAGES - 1; ++s) {
+            for (int s = 0; s < STAGES - 1; ++s) {
                 if (s < num_kt)
                     issue(s, s);
                 cp_async_commit();
             }
             for (int kt = 0; kt < num_kt; ++kt) {
-                cp_async_wait<FA_STAGES - 2>();
+                cp_async_wait<STAGES - 2>();
                 __syncthreads();
-                const int next = kt + FA_STAGES - 1;
+                const int next = kt + STAGES - 1;
                 if (next < num_kt)
-                    issue(next, next % FA_STAGES);
+                    issue(next, next % STAGES);
                 cp_async_commit();
-                const float *at = as + (kt % FA_STAGES) * T::kAStage;
-                const float *bt = bs + (kt % FA_STAGES) * T::kBStage;
+                const float *at = as + (kt % STAGES) * T::kAStage;
+                const float *bt = bs + (kt % STAGES) * T::kBStage;
 #pragma unroll
-                for (int k4 = 0; k4 < FA_BK; k4 += 4) {
+                for (int k4 = 0; k4 < BK; k4 += 4) {
                     float4 ar[RM];
 #pragma unroll
                     for (int i = 0; i < RM; ++i)
-                        ar[i] = *reinterpret_cast<const float4 *>(at + T::row(ty, i) * FA_A_LD + k4);
+                        ar[i] = *reinterpret_cast<const float4 *>(at + T::row(ty, i) * A_LD + k4);
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
                         float2 bp[RN / 2];

@@ -76,7 +76,7 @@ struct Context {
     int minor = 0;
     int sm_count = 0;
     int max_pairs = 0;        // co-resident 2-CTA clusters of the pair kernel
-    int ffma_resident[4] = {}; // resident blocks per SM of each aligned FFMA tile
+    int ffma_resident[2] = {}; // resident blocks per SM of each aligned FFMA tile
     EncodeTiledFn encode = nullptr;
     cudaMemPool_t pool = nullptr;
 };
@@ -491,19 +491,21 @@ void launch_ffma_kernel(const float *a, const float *b, float *c, int m, int k, 
 }
 
 // Launch plan of the aligned FFMA kernel: output tile and K split.  The busiest
-// SM's time is estimated as (its blocks) x (tile area) x (K tiles per split) /
-// efficiency, where efficiency falls when few warps are resident (the 8 x 8
-// micro-tiles saturate the FMA pipe from about 10 resident warps, a single
-// 4-warp block reaches about 65 % of that) and the 4 x 4 micro-tile pays 10 %
-// more shared-memory traffic per FMA; plus a fixed pipeline fill and epilogue
-// of two K tiles per wave of blocks.  Fitted to measured B200 times over square
-// sizes 64-4096 and skinny / long-K shapes (within 4 % of the best plan on
-// average, 15 % at worst).
+// SM's time is estimated as (its blocks) x (tile area) x (16-deep K steps per
+// split) / efficiency, where efficiency falls when fewer than about 14 warps are
+// resident and the 32 x 32 tile's 4 x 4 micro-tile is 25 % less efficient than
+// the 8 x 8 one; plus, per wave of resident blocks, a pipeline fill and epilogue
+// worth two K steps and, when split, a reduction worth one.  Fitted to measured
+// B200 times of every tile and split over square sizes 64-4096 and skinny /
+// long-K shapes (the chosen plan is within 3 % of the fastest on average, 14 %
+// at worst).  128 x 64 and 64 x 64 tiles were measured too and never won by
+// enough to keep.
 struct FfmaTileOption {
-    int bm, bn, warps;
+    int bm, bn, warps, bk;
     double efficiency;
 };
-constexpr FfmaTileOption kFfmaTiles[] = {{128, 128, 8, 1.0}, {128, 64, 4, 1.0}, {64, 64, 2, 0.9}, {32, 32, 2, 0.9}};
+constexpr FfmaTileOption kFfmaTiles[] = {{128, 128, 8, FaTile<128, 128, 8, 8>::kBK, 1.0},
+                                         {32, 32, 2, FaTile<32, 32, 4, 4>::kBK, 0.75}};
 constexpr int kFfmaTileCount = sizeof(kFfmaTiles) / sizeof(kFfmaTiles[0]);
 constexpr int kFfmaMaxSplits = 8;                       // portable cluster size
 
@@ -516,22 +518,24 @@ FfmaPlan choose_ffma_plan(int m, int k, int n, int sm_count, const int *resident
 {
     FfmaPlan best{0, 1};
     double best_cost = 0.0;
-    const int64_t total_kt = (static_cast<int64_t>(k) + FA_BK - 1) / FA_BK;
+    // Work in 16-deep K units; a split never has fewer K tiles of its own depth than one.
+    const int64_t total_kt = (static_cast<int64_t>(k) + FA_MODEL_BK - 1) / FA_MODEL_BK;
     for (int t = 0; t < kFfmaTileCount; ++t) {
         const FfmaTileOption &o = kFfmaTiles[t];
+        const int64_t tile_kt = (static_cast<int64_t>(k) + o.bk - 1) / o.bk;
         const int64_t tiles = ((static_cast<int64_t>(m) + o.bm - 1) / o.bm) *
                               ((static_cast<int64_t>(n) + o.bn - 1) / o.bn);
         const int64_t slots = resident[t] > 0 ? resident[t] : 1;
-        for (int splits = 1; splits <= kFfmaMaxSplits && splits <= total_kt; splits *= 2) {
+        for (int splits = 1; splits <= kFfmaMaxSplits && splits <= tile_kt; splits *= 2) {
             const int64_t per_sm = (tiles * splits + sm_count - 1) / sm_count;
             const int64_t concurrent = per_sm < slots ? per_sm : slots;
             const int64_t waves = (per_sm + slots - 1) / slots;
             const int64_t kt = (total_kt + splits - 1) / splits;
-            const double occupancy = 0.4 + static_cast<double>(concurrent * o.warps) / 16.0;
+            const double occupancy = 0.4 + static_cast<double>(concurrent * o.warps) / 24.0;
             const double efficiency = o.efficiency * (occupancy < 1.0 ? occupancy : 1.0);
             const double area = static_cast<double>(o.bm) * o.bn;
             const double cost = static_cast<double>(per_sm) * area * static_cast<double>(kt) / efficiency +
-                                2.0 * static_cast<double>(waves * concurrent) * area;
+                                (splits > 1 ? 3.0 : 2.0) * static_cast<double>(waves * concurrent) * area;
             if ((t == 0 && splits == 1) || cost < best_cost * 0.999) {
                 best = {t, splits};
                 best_cost = cost;
@@ -569,8 +573,6 @@ int launch_ffma(const Context *ctx, const float *a, const float *b, float *c, in
         cudaError_t st;
         switch (plan.tile) {
         case 0: st = launch_ffma_async<128, 128, 8, 8>(a, b, c, m, k, n, plan.splits, vc, stream); break;
-        case 1: st = launch_ffma_async<128, 64, 8, 8>(a, b, c, m, k, n, plan.splits, vc, stream); break;
-        case 2: st = launch_ffma_async<64, 64, 8, 8>(a, b, c, m, k, n, plan.splits, vc, stream); break;
         default: st = launch_ffma_async<32, 32, 4, 4>(a, b, c, m, k, n, plan.splits, vc, stream); break;
         }
         if (st != cudaSuccess)
@@ -652,11 +654,12 @@ extern "C" int matmul_kernel_info(int implementation, int precision, char *json,
             "\"tile_k\":%d,\"threads\":%d,\"warp_tile_m\":%d,\"warp_tile_n\":%d,\"microtile_m\":8,"
             "\"microtile_n\":8,\"buffering\":%d,\"load_method\":\"cp_async_16B_zero_fill\","
             "\"tensor_cores\":false,\"fma\":\"ffma2_rn_packed_fp32x2\",\"blocks_per_sm\":2,"
-            "\"small_tiles\":[[128,64,8,8],[64,64,8,8],[32,32,4,4]],\"split_k\":\"cluster_1x1xS_dsmem_reduce\","
+            "\"small_tiles\":[[32,32,4,4]],\"split_k\":\"cluster_1x1xS_dsmem_reduce\","
             "\"max_splits\":%d,\"plan_choice\":\"cost_model_busiest_sm\","
             "\"unaligned_kernel\":{\"tile_m\":%d,\"tile_n\":%d,\"tile_k\":%d,\"buffering\":2,"
             "\"load_method\":\"masked_scalar_register_prefetch\"}}",
-            FF_BM, FF_BN, FA_BK, FF_THREADS, 16, 128, FA_STAGES, kFfmaMaxSplits, FF_BM, FF_BN, FF_BK);
+            FF_BM, FF_BN, FaTile<128, 128, 8, 8>::kBK, FF_THREADS, 16, 128, FaTile<128, 128, 8, 8>::kStages,
+            kFfmaMaxSplits, FF_BM, FF_BN, FF_BK);
     }
     if (written < 0 || static_cast<size_t>(written) >= json_size) {
         json[0] = '\0';
@@ -744,8 +747,7 @@ extern "C" void *matmul_create(int device, char *error, size_t error_size)
             FaTile<BM, BN, RM, RN>::kSmemBytes                                                                   \
     }
     const std::pair<const void *, int> ffma_kernels[] = {
-        B200_FFMA_KERNEL(128, 128, 8, 8), B200_FFMA_KERNEL(128, 64, 8, 8), B200_FFMA_KERNEL(64, 64, 8, 8),
-        B200_FFMA_KERNEL(32, 32, 4, 4)};
+        B200_FFMA_KERNEL(128, 128, 8, 8), B200_FFMA_KERNEL(32, 32, 4, 4)};
 #undef B200_FFMA_KERNEL
     for (const auto &kernel : ffma_kernels) {
         st = cudaFuncSetAttribute(kernel.first, cudaFuncAttributeMaxDynamicSharedMemorySize, kernel.second);
