@@ -287,6 +287,26 @@ __device__ __forceinline__ float4 ld_shared_cluster_f4(uint32_t cluster_addr)
     return v;
 }
 
+// 16-byte store into the shared memory of a CTA of this cluster (a mapa address).
+__device__ __forceinline__ void st_shared_cluster_v4(uint32_t cluster_addr, uint32_t a, uint32_t b, uint32_t c,
+                                                     uint32_t d)
+{
+    asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_addr), "r"(a), "r"(b), "r"(c),
+                 "r"(d)
+                 : "memory");
+}
+
+// Bulk copy of `bytes` (a multiple of 16) from this CTA's shared memory into a
+// CTA of this cluster (`dst` and its mbarrier `bar` are mapa addresses); the
+// destination mbarrier receives the byte count as complete_tx.
+__device__ __forceinline__ void bulk_copy_to_cluster(uint32_t dst, uint32_t src, uint32_t bytes, uint32_t bar)
+{
+    asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     dst),
+                 "r"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
 // Every thread of every CTA in the cluster.
 __device__ __forceinline__ void cluster_sync_all()
 {

@@ -26,6 +26,16 @@
 // like A (MN-major TF32 would need the 32-byte-atom swizzle).  Tiles are
 // visited persistently (tile += gridDim.x) in groups of `group_m` M-blocks so
 // that concurrently running CTAs share A and B panels in L2.
+//
+// Split K (gridDim.z = S > 1, launched as clusters of (1, 1, S) with one tile per
+// cluster, gridDim.x = num_tiles): CTA z of a cluster runs K blocks
+// [z*ceil(nk/S), (z+1)*ceil(nk/S)) of the tile.  After a cluster barrier (every
+// operand ring idle) it writes its accumulator into its ring, bulk-copies rows
+// [j*128/S, (j+1)*128/S) into CTA j's shared memory (cp.async.bulk between the
+// CTAs of the cluster), and sums the S partials of its own rows in the fixed
+// order 0..S-1.  The partial and the S-1 received slices fit the ring plus the
+// epilogue staging area: S <= 4 for 256-wide tiles, S <= 8 otherwise.  Few output tiles over a long K otherwise leave most SMs idle and
+// the busy ones waiting on operand latency.
 #pragma once
 
 #include <cuda.h>
@@ -133,6 +143,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     constexpr uint32_t kBBoxBytes = kBK * TC_ROW_BYTES;  // bytes per B column block
     constexpr bool kBKMajor = kTF32;                     // TF32 B arrives transposed
     constexpr uint32_t kIdesc = tc_instr_desc(FMT, kBKMajor, TC_BM, BN);
+    // Split K: this CTA's 128 x BN FP32 partial, then up to S-1 received row
+    // slices, in the operand ring and the epilogue staging area behind it.
+    constexpr uint32_t kPartialRowBytes = BN * 4;
+    constexpr uint32_t kPartialBytes = TC_BM * kPartialRowBytes;
 
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_addr(smem_raw);
@@ -147,10 +161,17 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     auto acce_bar = [&](int i) { return s_bar + 8u * (2 * kStages + 2 + i); };
     const uint32_t drain_bar = s_bar + 8u * (2 * kStages + 4);
     const uint32_t tmem_slot = s_bar + 8u * (2 * kStages + 5);
+    const uint32_t recv_bar = s_bar + 8u * (2 * kStages + 6);   // split K: partial slices received
     uint32_t *tmem_slot_ptr = reinterpret_cast<uint32_t *>(smem_raw + (tmem_slot - raw));
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    // K blocks [kb_begin, kb_end) of this CTA's split (all of them when unsplit).
+    const int splits = static_cast<int>(gridDim.z);
+    const int kb_per_split = (p.num_k_blocks + splits - 1) / splits;
+    const int kb_begin = static_cast<int>(blockIdx.z) * kb_per_split;
+    const int kb_end = min(p.num_k_blocks, kb_begin + kb_per_split);
+    const bool has_k = kb_begin < kb_end;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -162,6 +183,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             mbar_init(acce_bar(i), 128);
         }
         mbar_init(drain_bar, 1);
+        mbar_init(recv_bar, 1);
         fence_mbarrier_init();
     }
     if (warp == 0 && lane == 0) {
@@ -191,7 +213,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
                 int mb, nb;
                 tc_tile_coords(tile, p, mb, nb);
-                for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+                for (int kb = kb_begin; kb < kb_end; ++kb) {
                     if (!mbar_wait(empty_bar(stage), phase ^ 1u)) {
                         report_status(kStatusLoadTimeout);
                         ok = false;
@@ -246,7 +268,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-                for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+                for (int kb = kb_begin; kb < kb_end; ++kb) {
                     if (!mbar_wait(full_bar(stage), phase)) {
                         report_status(kStatusMmaTimeout);
                         ok = false;
@@ -258,7 +280,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
 #pragma unroll
                     for (int kk = 0; kk < kMmasPerStage; ++kk)
                         tc_mma<kTF32>(d_tmem, a_desc + kk * kADescK, b_desc + kk * kBDescK, kIdesc,
-                                      (kb | kk) != 0 ? 1u : 0u);
+                                      (kb != kb_begin || kk != 0) ? 1u : 0u);
                     tc_commit(empty_bar(stage));
                     if (++stage == kStages) {
                         stage = 0;
@@ -267,7 +289,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 }
                 if (!ok)
                     break;
-                tc_commit(accf_bar(acc));
+                if (has_k)
+                    tc_commit(accf_bar(acc));
+                else
+                    mbar_arrive(accf_bar(acc));     // an empty split: its partial is zero
                 if (++acc == 2) {
                     acc = 0;
                     acc_phase ^= 1u;
@@ -302,6 +327,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             const int row0 = tile_row0 + quarter * 32;
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                    static_cast<uint32_t>(acc * BN);
+            if (splits > 1)
+                break;     // one tile; its accumulator is pushed to the owning CTAs below
 #pragma unroll 1
             for (int chunk = 0; chunk < BN / 32; ++chunk) {
                 uint32_t v[32];
@@ -353,6 +380,107 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         if (warp == 2 && lane == 0)
             bulk_wait_group_read<0>();     // shared memory free; the writes complete with the grid
         __syncwarp();
+    }
+
+    if (splits > 1 && kPartialBytes + static_cast<uint32_t>(splits - 1) * (kPartialBytes / splits) >
+                          static_cast<uint32_t>(kStages * (kAStage + kBStage) + TC_EPI_BYTES)) {
+        if (threadIdx.x == 0)
+            report_status(kStatusEpilogueTimeout);     // a launch the host never makes
+    } else if (splits > 1) {
+        // One tile per cluster.  Rows [j*rows, (j+1)*rows) of the tile are summed by
+        // CTA j.  Every CTA writes its accumulator into its own ring as a row-major
+        // partial (16-byte chunks XOR-swizzled by row), then the TMA engine copies
+        // each row slice to the CTA that owns it, into slot [sender, skipping the
+        // owner] behind the owner's partial; the owner adds the S slices in the
+        // order 0..S-1.
+        const int rows = TC_BM / splits;
+        const uint32_t slice_bytes = static_cast<uint32_t>(rows) * kPartialRowBytes;
+        const int z = static_cast<int>(blockIdx.z);
+        if (threadIdx.x == 0)
+            mbar_arrive_expect_tx(recv_bar, static_cast<uint32_t>(splits - 1) * slice_bytes);
+        cluster_sync_all();     // every CTA of the cluster is past its main loop: rings idle
+        if (warp >= 2) {
+            const int quarter = warp & 3;
+            const int r = quarter * 32 + lane;
+            const uint32_t row_addr = s_a + static_cast<uint32_t>(r) * kPartialRowBytes;
+            const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+#pragma unroll 1
+            for (int chunk = 0; chunk < BN / 32; ++chunk) {
+                uint32_t v[32];
+                if (has_k) {
+                    tmem_load_32cols(t_row + chunk * 32, v);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        v[j] = 0u;
+                }
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    st_shared_v4(row_addr + (((chunk * 8 + j) ^ (r & 7)) << 4), v[4 * j], v[4 * j + 1],
+                                 v[4 * j + 2], v[4 * j + 3]);
+            }
+            fence_proxy_async_shared();     // the bulk copies below read these stores
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            for (int j = 0; j < splits; ++j) {
+                if (j == z)
+                    continue;
+                const uint32_t slot = static_cast<uint32_t>(z < j ? z : z - 1);
+                bulk_copy_to_cluster(map_to_cta(s_a + kPartialBytes + slot * slice_bytes, static_cast<uint32_t>(j)),
+                                     s_a + static_cast<uint32_t>(j) * slice_bytes, slice_bytes,
+                                     map_to_cta(recv_bar, static_cast<uint32_t>(j)));
+            }
+        }
+        int received = 1;
+        if (lane == 0)
+            received = mbar_wait(recv_bar, 0) ? 1 : 0;
+        received = __shfl_sync(0xffffffffu, received, 0);
+        if (!received && lane == 0)
+            report_status(kStatusEpilogueTimeout);
+        int mb, nb;
+        tc_tile_coords(static_cast<int>(blockIdx.x), p, mb, nb);
+        const bool vec = !p.c_direct;
+        const uint8_t *ring = smem_raw + (s_a - raw);
+        for (int idx = threadIdx.x; received && idx < rows * (BN / 4); idx += TC_THREADS) {
+            const int rl = idx / (BN / 4), q = idx % (BN / 4);
+            const int r = z * rows + rl;                       // row within the tile
+            const uint32_t offset = static_cast<uint32_t>(rl) * kPartialRowBytes +
+                                    (static_cast<uint32_t>(q ^ (r & 7)) << 4);
+            float4 part[8];
+#pragma unroll
+            for (int src = 0; src < 8; ++src) {
+                if (src < splits) {
+                    const uint32_t base_off = src == z ? static_cast<uint32_t>(z) * slice_bytes
+                                                       : kPartialBytes + static_cast<uint32_t>(src < z ? src : src - 1) *
+                                                                             slice_bytes;
+                    part[src] = *reinterpret_cast<const float4 *>(ring + base_off + offset);
+                }
+            }
+            float4 sum = part[0];
+#pragma unroll
+            for (int src = 1; src < 8; ++src) {
+                if (src < splits) {
+                    sum.x += part[src].x;
+                    sum.y += part[src].y;
+                    sum.z += part[src].z;
+                    sum.w += part[src].w;
+                }
+            }
+            const int grow = mb * TC_BM + r, gcol = nb * BN + q * 4;
+            if (grow < p.m && gcol < p.n) {
+                float *dst = p.c + static_cast<size_t>(grow) * p.n + gcol;
+                if (vec && gcol + 3 < p.n) {
+                    *reinterpret_cast<float4 *>(dst) = sum;
+                } else {
+                    const float vals[4] = {sum.x, sum.y, sum.z, sum.w};
+                    for (int e = 0; e < 4 && gcol + e < p.n; ++e)
+                        dst[e] = vals[e];
+                }
+            }
+        }
+        // No CTA leaves while a copy into it (or out of it) may be in flight.
+        cluster_sync_all();
     }
 
     tc_fence_before();

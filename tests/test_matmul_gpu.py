@@ -122,6 +122,53 @@ def test_prepared_nondefault_stream_and_graph(native, backend, precision):
     del graph
 
 
+# Tensor-core shapes whose plans split K over clusters of 2, 4 and 8 CTAs (long K
+# against few output tiles), including a C that TMA cannot store (n % 4 != 0), an
+# unaligned K and m < 128.
+TC_SPLIT_SHAPES = ((1024, 4096, 1024), (512, 8192, 512), (96, 4096, 2048), (200, 3000, 300), (130, 4099, 258),
+                   (65, 2000, 70))
+
+
+def test_tcgen05_plans_split_k(native):
+    splits = set()
+    for precision in ("tf32", "fp16", "bf16"):
+        for shape in TC_SPLIT_SHAPES:
+            plan = native.plan("tcgen05", *shape, precision=precision)
+            assert plan["kernel"] == "tc_single"
+            splits.add(plan["splits"])
+    assert splits >= {2, 4, 8}
+    assert native.plan("tcgen05", 8192, 8192, 8192, precision="bf16")["kernel"] == "tc2_pair"
+
+
+@pytest.mark.parametrize("precision", ("tf32", "fp16", "bf16"))
+@pytest.mark.parametrize("shape", TC_SPLIT_SHAPES)
+def test_tcgen05_split_k_against_fp64_oracle(native, precision, shape):
+    m, k, n = shape
+    a_np = po.seeded_uniform((m, k), seed=11 * m + k)
+    b_np = po.seeded_uniform((k, n), seed=13 * n + k)
+    _run_and_verify(native, "tcgen05", precision, a_np, b_np, offset=False)
+
+
+def test_tcgen05_split_k_is_deterministic_and_graph_capturable(native):
+    m, k, n = 512, 8192, 512
+    assert native.plan("tcgen05", m, k, n, precision="bf16")["splits"] > 1
+    a = torch.from_numpy(po.seeded_uniform((m, k), 3)).cuda().to(torch.bfloat16)
+    b = torch.from_numpy(po.seeded_uniform((k, n), 4)).cuda().to(torch.bfloat16)
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        first = torch.empty((m, n), device="cuda")
+        second = torch.full((m, n), float("nan"), device="cuda")
+        native.prepare("tcgen05", a, b, first, precision="bf16")()
+        run = native.prepare("tcgen05", a, b, second, precision="bf16")
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            run()
+        graph.replay()
+        stream.synchronize()
+    assert torch.equal(first, second)
+    del graph
+
+
 # Aligned FP32 shapes whose launch plans (matmul_plan) cover both FFMA tiles and
 # K splits of 1, 2, 4 and 8 cluster CTAs, including splits that get no K tiles
 # (32 x 144 x 32: 9 K tiles over 8 CTAs).
