@@ -200,33 +200,42 @@ void launch_pack(const void *src, void *dst, int64_t rows, int64_t cols, int64_t
 }
 
 // TF32 B: dst (n x ld) = rounded transpose of src (k x n).
-void transpose_round_b(const void *src, void *dst, int64_t k, int64_t n, int64_t ld, cudaStream_t stream)
+// Both TF32 operands in one launch: rounded A (m x lda) and rounded, transposed B
+// (n x ldb), each into 16-byte aligned scratch.
+cudaError_t prepare_tf32(const Context *ctx, const float *a, float *a_dst, int64_t m, int64_t k, int64_t lda,
+                         const float *b, float *b_dst, int64_t n, int64_t ldb, cudaStream_t stream)
 {
-    const int64_t nt = (n + 31) / 32, kt = (ld + 31) / 32;
-    const dim3 grid(static_cast<unsigned int>(nt < 4096 ? nt : 4096), static_cast<unsigned int>(kt < 4096 ? kt : 4096));
-    transpose_round_tf32_kernel<<<grid, dim3(32, 8), 0, stream>>>(static_cast<const float *>(src),
-                                                                  static_cast<float *>(dst), k, n, ld);
+    Tf32Prep prep{};
+    prep.a = a;
+    prep.a_dst = a_dst;
+    prep.b = b;
+    prep.b_dst = b_dst;
+    prep.m = m;
+    prep.k = k;
+    prep.n = n;
+    prep.lda = lda;
+    prep.ldb = ldb;
+    prep.a_vec = aligned16(a) && lda == k ? 1 : 0;
+    prep.b_vec = aligned16(b) && n % 4 == 0 ? 1 : 0;
+    const int64_t a_work = prep.a_vec ? m * k / 4 : m * lda;
+    const int64_t a_cap = 4LL * ctx->sm_count, b_cap = 8LL * ctx->sm_count;
+    int64_t a_blocks = (a_work + 255) / 256;
+    a_blocks = a_blocks < 1 ? 1 : a_blocks > a_cap ? a_cap : a_blocks;
+    int64_t b_blocks = ((n + TP_TILE - 1) / TP_TILE) * ((ldb + TP_TILE - 1) / TP_TILE);
+    b_blocks = b_blocks < 1 ? 1 : b_blocks > b_cap ? b_cap : b_blocks;
+    prep.a_blocks = static_cast<int>(a_blocks);
+    return launch_pdl(tf32_prepare_kernel, dim3(static_cast<unsigned int>(a_blocks + b_blocks)), dim3(256), 0,
+                      stream, prep);
 }
 
-// Prepare one operand for TMA (copy with padding and/or TF32 rounding into scratch).
+// Prepare one FP16/BF16 operand for TMA (copy with zero padding into scratch).
 void prepare_operand(int prec, const void *src, int64_t rows, int64_t cols, bool direct, void *scratch,
                      int64_t ld, const Context *ctx, cudaStream_t stream)
 {
+    (void)ctx;
     if (direct)
         return;
-    if (prec == kPrecTf32) {
-        if (ld == cols && aligned16(src)) {
-            const int64_t count4 = rows * cols / 4;
-            const int64_t blocks = (count4 + 255) / 256;
-            const unsigned int grid =
-                static_cast<unsigned int>(blocks < 8LL * ctx->sm_count ? (blocks < 1 ? 1 : blocks)
-                                                                       : 8LL * ctx->sm_count);
-            round_tf32_vec_kernel<<<grid, 256, 0, stream>>>(static_cast<const float4 *>(src),
-                                                            static_cast<float4 *>(scratch), count4);
-        } else {
-            launch_pack<float, true>(src, scratch, rows, cols, ld, stream);
-        }
-    } else if (prec == kPrecBf16) {
+    if (prec == kPrecBf16) {
         launch_pack<__nv_bfloat16, false>(src, scratch, rows, cols, ld, stream);
     } else {
         launch_pack<__half, false>(src, scratch, rows, cols, ld, stream);
@@ -461,11 +470,19 @@ int launch_tcgen05(Context *ctx, int prec, const void *a, const void *b, float *
     void *pooled = fixed_scratch ? nullptr : scratch;
     const void *a_op = a_direct ? a : scratch;
     const void *b_op = b_direct ? b : static_cast<uint8_t *>(scratch) + a_bytes;
-    prepare_operand(prec, a, m, k, a_direct, const_cast<void *>(a_op), lda, ctx, stream);
-    if (b_transposed)
-        transpose_round_b(b, const_cast<void *>(b_op), k, n, ldb, stream);
-    else
+    if (prec == kPrecTf32) {
+        const cudaError_t st = prepare_tf32(ctx, static_cast<const float *>(a), static_cast<float *>(const_cast<void *>(a_op)),
+                                            m, k, lda, static_cast<const float *>(b),
+                                            static_cast<float *>(const_cast<void *>(b_op)), n, ldb, stream);
+        if (st != cudaSuccess) {
+            if (pooled)
+                cudaFreeAsync(pooled, stream);
+            return fail(error, error_size, "kernel launch", cudaGetErrorString(st));
+        }
+    } else {
+        prepare_operand(prec, a, m, k, a_direct, const_cast<void *>(a_op), lda, ctx, stream);
         prepare_operand(prec, b, k, n, b_direct, const_cast<void *>(b_op), ldb, ctx, stream);
+    }
 
     if (m <= kSkinnyMaxM) {
         const int rc = launch_skinny(ctx, prec, a_op, lda, b_op, ldb, b_transposed, c, m, k, n, stream, error,
