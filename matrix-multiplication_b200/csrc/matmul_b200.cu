@@ -353,24 +353,33 @@ TcPlan choose_tc_plan(const Context *ctx, int m, int k, int n, int prec)
     return best;
 }
 
-// Two K halves when the 128-column slabs alone would leave half the SMs idle.
+// K splits of the skinny kernel: the most (1, 2, 4 or 8) whose clusters all fit
+// on the device at once with at least four K blocks per split.  The kernel is
+// HBM-bound on B, so more SMs streaming it is what counts.
 int skinny_splits(const Context *ctx, int n, int total_k_blocks)
 {
-    const int tiles = (n + SK_BM - 1) / SK_BM;
-    return (2 * tiles <= ctx->sm_count && total_k_blocks >= 4) ? 2 : 1;
+    const int64_t tiles = (n + SK_BM - 1) / SK_BM;
+    int best = 1;
+    for (int i = 1; i < 4; ++i) {
+        const int splits = 1 << i;
+        const int64_t kpb = (total_k_blocks + splits - 1) / splits;
+        if (tiles * splits <= ctx->max_split_ctas[i] && kpb >= 4 && (splits - 1) * kpb < total_k_blocks)
+            best = splits;
+    }
+    return best;
 }
 
 template <int FMT, int NP>
-cudaError_t launch_skinny_kernel(const CUtensorMap &mbt, const CUtensorMap &mat, const SkParams &params, int grid,
+cudaError_t launch_skinny_kernel(const CUtensorMap &mbt, const CUtensorMap &mat, const SkParams &params, dim3 grid,
                                  cudaStream_t stream)
 {
-    return launch_pdl(tc_skinny_kernel<FMT, NP>, dim3(grid), dim3(TC_THREADS), SkTile<NP>::kSmem, stream, mbt, mat,
-                      params);
+    return launch_pdl_cluster_z(tc_skinny_kernel<FMT, NP>, grid, dim3(TC_THREADS), SkTile<NP>::kSmem, grid.z, stream,
+                                mbt, mat, params);
 }
 
 template <int FMT>
 cudaError_t launch_skinny_np(int np, const CUtensorMap &mbt, const CUtensorMap &mat, const SkParams &params,
-                             int grid, cudaStream_t stream)
+                             dim3 grid, cudaStream_t stream)
 {
     if (np == 16)
         return launch_skinny_kernel<FMT, 16>(mbt, mat, params, grid, stream);
@@ -412,16 +421,15 @@ int launch_skinny(Context *ctx, int prec, const void *a_op, int64_t lda, const v
     params.k = k;
     params.num_n_tiles = (n + SK_BM - 1) / SK_BM;
     params.total_k_blocks = static_cast<int>((static_cast<int64_t>(k) + bk - 1) / bk);
-    params.splits = skinny_splits(ctx, n, params.total_k_blocks);
-    params.num_k_blocks = (params.total_k_blocks + params.splits - 1) / params.splits;
-    params.num_tiles = params.num_n_tiles * params.splits;
+    const int splits = skinny_splits(ctx, n, params.total_k_blocks);
+    params.num_k_blocks = (params.total_k_blocks + splits - 1) / splits;
     params.c = c;
-    if (params.splits > 1) {
-        const cudaError_t st = cudaMemsetAsync(c, 0, static_cast<size_t>(m) * n * sizeof(float), stream);
-        if (st != cudaSuccess)
-            return fail_cuda(error, error_size, "matmul_launch: cudaMemsetAsync", st);
-    }
-    const int grid = params.num_tiles < ctx->sm_count ? params.num_tiles : ctx->sm_count;
+    // Split K: one 128-column slab per cluster of `splits` CTAs along z.
+    const dim3 grid = splits > 1 ? dim3(static_cast<unsigned int>(params.num_n_tiles), 1,
+                                        static_cast<unsigned int>(splits))
+                                 : dim3(static_cast<unsigned int>(params.num_n_tiles < ctx->sm_count
+                                                                      ? params.num_n_tiles
+                                                                      : ctx->sm_count));
     cudaError_t st;
     if (prec == kPrecTf32)
         st = launch_skinny_np<kFmtTF32>(np, map_bt, map_at, params, grid, stream);

@@ -12,10 +12,12 @@
 //   * TMEM: 128 lanes (n) x NP columns (m), two accumulators.
 //   * Epilogue: each warp loads 16 columns (m) of its 32 lanes (n) and writes, per
 //     m, 32 consecutive floats of C's row m (one 128-byte store per warp per row).
-//   * Split K in two when there are too few 128-column slabs to occupy the GPU:
-//     both halves add into a zeroed C with float atomics.  Exactly two additions
-//     per output make the result independent of their order (FP32 addition is
-//     commutative), so the output is deterministic.
+//   * Split K when there are too few 128-column slabs to occupy the GPU: a
+//     launch with gridDim.z = S > 1 forms clusters of (1, 1, S), one slab per
+//     cluster; CTA z streams K blocks [z*ceil(nk/S), (z+1)*ceil(nk/S)), writes its
+//     128 x NP FP32 partial into its idle ring, bulk-copies the rows (columns n)
+//     [j*128/S, (j+1)*128/S) to CTA j, and sums the S partials of its own rows in
+//     the fixed order 0..S-1 (deterministic, no zeroing of C, no atomics).
 // Warp roles and bounded waits as in tc_gemm.cuh.
 #pragma once
 
@@ -42,10 +44,8 @@ struct SkTile {
 struct SkParams {
     int m, n, k;
     int num_n_tiles;          // 128-column slabs of C
-    int splits;               // 1 or 2 halves of K
-    int num_k_blocks;         // K blocks per split
+    int num_k_blocks;         // K blocks per split (all of them when gridDim.z == 1)
     int total_k_blocks;
-    int num_tiles;            // num_n_tiles * splits
     float *c;
 };
 
@@ -84,10 +84,19 @@ tc_skinny_kernel(const __grid_constant__ CUtensorMap map_bt, const __grid_consta
     auto acce_bar = [&](int i) { return s_bar + 8u * (2 * kStages + 2 + i); };
     const uint32_t drain_bar = s_bar + 8u * (2 * kStages + 4);
     const uint32_t tmem_slot = s_bar + 8u * (2 * kStages + 5);
+    const uint32_t recv_bar = s_bar + 8u * (2 * kStages + 6);   // split K: partial rows received
     uint32_t *tmem_slot_ptr = reinterpret_cast<uint32_t *>(smem_raw + (tmem_slot - raw));
+    // Split K: 128 x NP FP32 partial rows (n) padded to NP + 4 floats, then the
+    // S-1 received slices, in the idle operand ring.
+    constexpr uint32_t kPartialPitch = (NP + 4) * 4;
+    constexpr uint32_t kPartialBytes = SK_BM * kPartialPitch;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    const int splits = static_cast<int>(gridDim.z);
+    const int split = static_cast<int>(blockIdx.z);
+    const int kb0 = split * p.num_k_blocks;
+    const int kb1 = min(kb0 + p.num_k_blocks, p.total_k_blocks);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -99,6 +108,7 @@ tc_skinny_kernel(const __grid_constant__ CUtensorMap map_bt, const __grid_consta
             mbar_init(acce_bar(i), 128);
         }
         mbar_init(drain_bar, 1);
+        mbar_init(recv_bar, 1);
         fence_mbarrier_init();
     }
     if (warp == 0 && lane == 0) {
@@ -123,11 +133,7 @@ tc_skinny_kernel(const __grid_constant__ CUtensorMap map_bt, const __grid_consta
             uint32_t phase = 0;
             uint32_t filled = 0, fill_parity = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
-                const int nt = tile % p.num_n_tiles;
-                const int split = tile / p.num_n_tiles;
-                const int kb0 = split * p.num_k_blocks;
-                const int kb1 = min(kb0 + p.num_k_blocks, p.total_k_blocks);
+            for (int nt = blockIdx.x; ok && nt < p.num_n_tiles; nt += gridDim.x) {
                 for (int kb = kb0; kb < kb1; ++kb) {
                     if (!mbar_wait(empty_bar(stage), phase ^ 1u)) {
                         report_status(kStatusLoadTimeout);
@@ -172,10 +178,7 @@ tc_skinny_kernel(const __grid_constant__ CUtensorMap map_bt, const __grid_consta
             int acc = 0;
             uint32_t acc_phase = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
-                const int split = tile / p.num_n_tiles;
-                const int kb0 = split * p.num_k_blocks;
-                const int kb1 = min(kb0 + p.num_k_blocks, p.total_k_blocks);
+            for (int nt = blockIdx.x; ok && nt < p.num_n_tiles; nt += gridDim.x) {
                 if (!mbar_wait(acce_bar(acc), acc_phase ^ 1u)) {
                     report_status(kStatusMmaTimeout);
                     break;
@@ -203,7 +206,10 @@ tc_skinny_kernel(const __grid_constant__ CUtensorMap map_bt, const __grid_consta
                 }
                 if (!ok)
                     break;
-                tc_commit(accf_bar(acc));
+                if (kb0 < kb1)
+                    tc_commit(accf_bar(acc));
+                else
+                    mbar_arrive(accf_bar(acc));     // an empty split: its partial is zero
                 if (++acc == 2) {
                     acc = 0;
                     acc_phase ^= 1u;
@@ -219,8 +225,7 @@ tc_skinny_kernel(const __grid_constant__ CUtensorMap map_bt, const __grid_consta
         const int quarter = warp & 3;                 // TMEM lanes = columns n of C
         int acc = 0;
         uint32_t acc_phase = 0;
-        for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
-            const int nt = tile % p.num_n_tiles;
+        for (int nt = blockIdx.x; nt < p.num_n_tiles; nt += gridDim.x) {
             int ok = 1;
             if (lane == 0)
                 ok = mbar_wait(accf_bar(acc), acc_phase) ? 1 : 0;
@@ -231,6 +236,8 @@ tc_skinny_kernel(const __grid_constant__ CUtensorMap map_bt, const __grid_consta
                 break;
             }
             tc_fence_after();
+            if (splits > 1)
+                break;     // one slab; its partial is exchanged below
             const int col = nt * SK_BM + quarter * 32 + lane;
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                    static_cast<uint32_t>(acc * NP);
@@ -246,13 +253,8 @@ tc_skinny_kernel(const __grid_constant__ CUtensorMap map_bt, const __grid_consta
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
                         const int row = chunk * 16 + j;
-                        if (row < p.m) {
-                            float *dst = p.c + static_cast<size_t>(row) * p.n + col;
-                            if (p.splits == 1)
-                                *dst = __uint_as_float(v[j]);
-                            else
-                                atomicAdd(dst, __uint_as_float(v[j]));
-                        }
+                        if (row < p.m)
+                            p.c[static_cast<size_t>(row) * p.n + col] = __uint_as_float(v[j]);
                     }
                 }
             }
@@ -262,6 +264,78 @@ tc_skinny_kernel(const __grid_constant__ CUtensorMap map_bt, const __grid_consta
             }
         }
         __syncwarp();
+    }
+
+    if (splits > 1 && kPartialBytes + static_cast<uint32_t>(splits - 1) * (kPartialBytes / splits) >
+                          static_cast<uint32_t>(kStages * (kAStage + kBStage))) {
+        if (threadIdx.x == 0)
+            report_status(kStatusEpilogueTimeout);     // a launch the host never makes
+    } else if (splits > 1) {
+        const int rows = SK_BM / splits;                 // columns n of the slab summed by each CTA
+        const uint32_t slice_bytes = static_cast<uint32_t>(rows) * kPartialPitch;
+        const int nt = static_cast<int>(blockIdx.x);
+        if (threadIdx.x == 0)
+            mbar_arrive_expect_tx(recv_bar, static_cast<uint32_t>(splits - 1) * slice_bytes);
+        cluster_sync_all();     // every CTA of the cluster is past its main loop: rings idle
+        if (warp >= 2) {
+            const int quarter = warp & 3;
+            const uint32_t row_addr = s_a + static_cast<uint32_t>(quarter * 32 + lane) * kPartialPitch;
+            const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+#pragma unroll 1
+            for (int chunk = 0; chunk < NP / 16; ++chunk) {
+                uint32_t v[16];
+                if (kb0 < kb1) {
+                    tmem_load_16cols(t_row + chunk * 16, v);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        v[j] = 0u;
+                }
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    st_shared_v4(row_addr + (chunk * 16 + 4 * j) * 4, v[4 * j], v[4 * j + 1], v[4 * j + 2],
+                                 v[4 * j + 3]);
+            }
+            fence_proxy_async_shared();     // the bulk copies below read these stores
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            for (int j = 0; j < splits; ++j) {
+                if (j == split)
+                    continue;
+                const uint32_t slot = static_cast<uint32_t>(split < j ? split : split - 1);
+                bulk_copy_to_cluster(map_to_cta(s_a + kPartialBytes + slot * slice_bytes, static_cast<uint32_t>(j)),
+                                     s_a + static_cast<uint32_t>(j) * slice_bytes, slice_bytes,
+                                     map_to_cta(recv_bar, static_cast<uint32_t>(j)));
+            }
+        }
+        int received = 1;
+        if (lane == 0)
+            received = mbar_wait(recv_bar, 0) ? 1 : 0;
+        received = __shfl_sync(0xffffffffu, received, 0);
+        if (!received && lane == 0)
+            report_status(kStatusEpilogueTimeout);
+        const uint8_t *ring = smem_raw + (s_a - raw);
+        for (int idx = threadIdx.x; received && idx < p.m * rows; idx += TC_THREADS) {
+            const int row = idx / rows, rl = idx % rows;    // C row (m), column offset within the slice
+            const uint32_t offset = static_cast<uint32_t>(rl) * kPartialPitch + static_cast<uint32_t>(row) * 4;
+            float sum = 0.0f;
+#pragma unroll
+            for (int src = 0; src < 8; ++src) {
+                if (src < splits) {
+                    const uint32_t base_off =
+                        src == split ? static_cast<uint32_t>(split) * slice_bytes
+                                     : kPartialBytes + static_cast<uint32_t>(src < split ? src : src - 1) * slice_bytes;
+                    const float v = *reinterpret_cast<const float *>(ring + base_off + offset);
+                    sum = src == 0 ? v : sum + v;
+                }
+            }
+            const int col = nt * SK_BM + split * rows + rl;
+            if (col < p.n)
+                p.c[static_cast<size_t>(row) * p.n + col] = sum;
+        }
+        // No CTA leaves while a copy into it (or out of it) may be in flight.
+        cluster_sync_all();
     }
 
     tc_fence_before();

@@ -129,6 +129,26 @@ TC_SPLIT_SHAPES = ((1024, 4096, 1024), (512, 8192, 512), (96, 4096, 2048), (200,
                    (65, 2000, 70))
 
 
+SKINNY_SPLIT_SHAPES = ((16, 8192, 1024), (48, 4096, 2048), (5, 3000, 260), (64, 2048, 8192), (32, 1024, 4096))
+
+
+def test_skinny_plans_split_k(native):
+    assert native.plan("tcgen05", 16, 8192, 8192, precision="bf16") == {
+        "kernel": "tc_skinny", "tile_m": 16, "tile_n": 128, "splits": 2}
+    splits = {native.plan("tcgen05", *shape, precision=p)["splits"]
+              for shape in SKINNY_SPLIT_SHAPES for p in ("tf32", "fp16", "bf16")}
+    assert splits >= {2, 4, 8}
+
+
+@pytest.mark.parametrize("precision", ("tf32", "fp16", "bf16"))
+@pytest.mark.parametrize("shape", SKINNY_SPLIT_SHAPES)
+def test_skinny_split_k_against_fp64_oracle(native, precision, shape):
+    m, k, n = shape
+    a_np = po.seeded_uniform((m, k), seed=17 * m + k)
+    b_np = po.seeded_uniform((k, n), seed=19 * n + k)
+    _run_and_verify(native, "tcgen05", precision, a_np, b_np, offset=False)
+
+
 def test_tcgen05_plans_split_k(native):
     splits = set()
     for precision in ("tf32", "fp16", "bf16"):
