@@ -729,13 +729,15 @@ extern "C" int matmul_kernel_info(int implementation, int precision, char *json,
             "\"accumulator\":\"tmem_fp32\",\"tmem_columns\":%u,\"accumulator_buffers\":2,"
             "\"warp_roles\":{\"tma\":1,\"mma\":1,\"epilogue\":4},\"schedule\":\"persistent\","
             "\"raster_group_m\":%d,\"epilogue\":\"tmem_ld_smem_tma_store\",\"input_rounding\":\"%s\","
-            "\"b_operand\":\"%s\",\"single_cta_kernel\":{\"when\":\"pair tiles < one wave\",\"tile_m\":%d,"
-            "\"tile_n\":[256,128,64],\"buffering\":[%d,%d,%d],\"raster_group_m\":%d}}",
+            "\"b_operand\":\"%s\",\"plan\":\"cost_model\",\"single_cta_kernel\":{\"tile_m\":%d,"
+            "\"tile_n\":[256,128,64],\"buffering\":[%d,%d,%d],\"raster_group_m\":%d,"
+            "\"split_k\":\"cluster_1x1xS_bulk_copy\",\"max_splits\":8},"
+            "\"skinny_kernel\":{\"when\":\"m<=64\",\"tile_n\":%d,\"max_splits\":8}}",
             kPrecisionNames[precision], TC2_BM, TC2_BN, TC_ROW_BYTES / elem, TC_THREADS, TC2_HALF, TC2_BN, TC2_HALF,
             TC2_BN, TC2_STAGES, precision == kPrecTf32 ? "tf32" : "f16", TC2_BM, TC2_BN, 32 / elem,
             TC_TMEM_COLUMNS, kRasterGroupMPair, precision == kPrecTf32 ? "rne_prepass" : "none",
             precision == kPrecTf32 ? "k_major_rounded_transpose" : "mn_major_tma", TC_BM, TcTile<256>::kStages,
-            TcTile<128>::kStages, TcTile<64>::kStages, kRasterGroupM);
+            TcTile<128>::kStages, TcTile<64>::kStages, kRasterGroupM, SK_BM);
     } else {
         written = std::snprintf(
             json, json_size,
