@@ -4,21 +4,19 @@
 // Replaces the reference's FP32 kernels (matmul_tiled_fp32 / matmul_register_fp32
 // in src/matmul.cu:73-195 and matmul_warp_fp32 in src/matmul_custom.cuh:85-156)
 // with one register-blocked kernel:
-//   * 128 x 128 output tile per 256-thread block, K step 8, two blocks per SM;
-//   * each thread owns an 8 x 8 micro-tile split into 2 x 2 groups of 4 x 4 that
-//     are 64 rows / columns apart, so every shared-memory operand read is a
-//     conflict-free float4 and each warp's B reads are two 128-byte rows;
-//   * A is stored transposed (k-major) in shared memory, B as is;
-//   * three levels of double buffering: the next K tile is fetched from global
-//     memory into registers, the shared tiles alternate between two buffers
-//     (one barrier per K step), and the register fragments of k-slice kk+1 are
-//     read from shared memory while the 64 FMAs of slice kk execute, so shared
-//     load latency never sits on the FFMA issue path;
-//   * the 64 multiply-adds of a k-slice are 32 packed FP32x2 FMAs (sm_100's
-//     paired FFMA: two IEEE FMAs, round to nearest, per issued instruction),
-//     so instruction issue no longer caps the FMA pipe;
-//   * float4 global loads/stores when rows are 16-byte aligned, guarded scalar
-//     accesses otherwise (offset base pointers, odd k or n, partial tiles).
+//   * a 3- or 4-stage cp.async pipeline feeds shared memory straight from global
+//     memory (no register staging, one barrier per 16- or 32-deep K tile): 16-byte
+//     copies when A and B rows are 16-byte aligned (k % 4 == 0, n % 4 == 0,
+//     aligned bases), 4-byte copies otherwise (offset bases, odd k or n); partial
+//     tiles are zero-filled by cp.async's source-size operand;
+//   * A stays row-major in shared memory (rows padded by 4 floats) and is read as
+//     float4 along k, so one A fragment load serves four k-slices; B is read as
+//     float4 along n;
+//   * the multiply-adds are packed FP32x2 FMAs (__ffma2_rn: two IEEE
+//     round-to-nearest FMAs per issued instruction), so instruction issue does
+//     not cap the FMA pipe;
+//   * float4 stores of C when its rows are 16-byte aligned, guarded scalar
+//     stores otherwise.
 #pragma once
 
 #include <cstdint>
@@ -29,184 +27,8 @@ namespace b200 {
 
 constexpr int FF_BM = 128;
 constexpr int FF_BN = 128;
-constexpr int FF_BK = 8;
 constexpr int FF_THREADS = 256;
 
-template <bool VEC_A, bool VEC_B, bool VEC_C>
-__global__ void __launch_bounds__(FF_THREADS, 2)
-ffma_gemm_kernel(const float *__restrict__ a, const float *__restrict__ b, float *__restrict__ c, int m,
-                 int n, int k)
-{
-    __shared__ __align__(16) float as[2][FF_BK][FF_BM];
-    __shared__ __align__(16) float bs[2][FF_BK][FF_BN];
-
-    wait_for_prior_grid();
-    allow_next_grid();
-    const int tid = threadIdx.x;
-    const int tx = tid & 15;                 // column group
-    const int ty = tid >> 4;                 // row group
-    // Global -> shared mapping.  A: each thread loads kAVec float4s (consecutive k)
-    // of one row; a warp covers 32 rows at the same k offset, so the transposed
-    // shared stores are conflict-free.
-    constexpr int kAVec = FF_BK / 8;
-    const int a_row = tid & 127;
-    const int a_k = (tid >> 7) * 4 * kAVec;
-    // B: each thread loads kBVec float4s of row b_k at columns b_col + 32 q
-    // (a warp covers 128 contiguous columns per store: conflict-free).
-    constexpr int kBVec = FF_BK / 8;
-    const int b_k = (tid >> 5) * kBVec;
-    const int b_col = (tid & 31) * 4;
-    const int num_kt = (k + FF_BK - 1) / FF_BK;
-
-    for (int block_m = blockIdx.y; block_m * FF_BM < m; block_m += gridDim.y) {
-        for (int block_n = blockIdx.x; block_n * FF_BN < n; block_n += gridDim.x) {
-            const int m0 = block_m * FF_BM;
-            const int n0 = block_n * FF_BN;
-            const int grow = m0 + a_row;
-            const bool a_row_ok = grow < m;
-            const float *a_ptr = a + static_cast<size_t>(a_row_ok ? grow : 0) * k;
-            const int bcol = n0 + b_col;
-
-            float ra[4 * kAVec];
-            float rb[4 * kBVec];
-            auto fetch = [&](int kt) {
-#pragma unroll
-                for (int h = 0; h < kAVec; ++h) {
-                    const int kk = kt * FF_BK + a_k + 4 * h;
-                    if (VEC_A && a_row_ok && kk + 3 < k) {
-                        const float4 v = *reinterpret_cast<const float4 *>(a_ptr + kk);
-                        ra[4 * h] = v.x;
-                        ra[4 * h + 1] = v.y;
-                        ra[4 * h + 2] = v.z;
-                        ra[4 * h + 3] = v.w;
-                    } else {
-#pragma unroll
-                        for (int q = 0; q < 4; ++q)
-                            ra[4 * h + q] = (a_row_ok && kk + q < k) ? a_ptr[kk + q] : 0.0f;
-                    }
-                }
-#pragma unroll
-                for (int h = 0; h < kBVec; ++h) {
-                    const int krow = kt * FF_BK + b_k + h;
-                    const bool k_ok = krow < k;
-                    const float *b_ptr = b + static_cast<size_t>(k_ok ? krow : 0) * n;
-                    if (VEC_B && k_ok && bcol + 3 < n) {
-                        const float4 v = *reinterpret_cast<const float4 *>(b_ptr + bcol);
-                        rb[4 * h] = v.x;
-                        rb[4 * h + 1] = v.y;
-                        rb[4 * h + 2] = v.z;
-                        rb[4 * h + 3] = v.w;
-                    } else {
-#pragma unroll
-                        for (int q = 0; q < 4; ++q)
-                            rb[4 * h + q] = (k_ok && bcol + q < n) ? b_ptr[bcol + q] : 0.0f;
-                    }
-                }
-            };
-            auto stash = [&](int buf) {
-#pragma unroll
-                for (int q = 0; q < 4 * kAVec; ++q)
-                    as[buf][a_k + q][a_row] = ra[q];
-#pragma unroll
-                for (int h = 0; h < kBVec; ++h)
-                    *reinterpret_cast<float4 *>(&bs[buf][b_k + h][b_col]) =
-                        make_float4(rb[4 * h], rb[4 * h + 1], rb[4 * h + 2], rb[4 * h + 3]);
-            };
-
-            // acc[i][p] holds outputs (i, 2p) and (i, 2p + 1): one packed FP32x2 FMA
-            // (__ffma2_rn, two IEEE round-to-nearest FMAs per instruction) updates both.
-            float2 acc[8][4];
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    acc[i][j] = make_float2(0.0f, 0.0f);
-
-            float fa[2][8];
-            float fb[2][8];
-            auto load_frag = [&](int buf, int kk, int slot) {
-                const float4 a0 = *reinterpret_cast<const float4 *>(&as[buf][kk][ty * 4]);
-                const float4 a1 = *reinterpret_cast<const float4 *>(&as[buf][kk][64 + ty * 4]);
-                const float4 b0 = *reinterpret_cast<const float4 *>(&bs[buf][kk][tx * 4]);
-                const float4 b1 = *reinterpret_cast<const float4 *>(&bs[buf][kk][64 + tx * 4]);
-                fa[slot][0] = a0.x; fa[slot][1] = a0.y; fa[slot][2] = a0.z; fa[slot][3] = a0.w;
-                fa[slot][4] = a1.x; fa[slot][5] = a1.y; fa[slot][6] = a1.z; fa[slot][7] = a1.w;
-                fb[slot][0] = b0.x; fb[slot][1] = b0.y; fb[slot][2] = b0.z; fb[slot][3] = b0.w;
-                fb[slot][4] = b1.x; fb[slot][5] = b1.y; fb[slot][6] = b1.z; fb[slot][7] = b1.w;
-            };
-
-            fetch(0);
-            stash(0);
-            __syncthreads();
-            load_frag(0, 0, 0);
-            int buf = 0;
-            for (int kt = 0; kt < num_kt; ++kt) {
-                const bool more = kt + 1 < num_kt;
-                if (more)
-                    fetch(kt + 1);
-#pragma unroll
-                for (int kk = 0; kk < FF_BK; ++kk) {
-                    const int cur = kk & 1;
-                    if (kk == FF_BK - 1) {
-                        // Publish the next tile, then read its first slice.
-                        if (more) {
-                            stash(buf ^ 1);
-                            __syncthreads();
-                            load_frag(buf ^ 1, 0, cur ^ 1);
-                        }
-                    } else {
-                        load_frag(buf, kk + 1, cur ^ 1);
-                    }
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        const float2 ai = make_float2(fa[cur][i], fa[cur][i]);
-#pragma unroll
-                        for (int j = 0; j < 4; ++j)
-                            acc[i][j] = __ffma2_rn(ai, make_float2(fb[cur][2 * j], fb[cur][2 * j + 1]), acc[i][j]);
-                    }
-                }
-                buf ^= 1;
-            }
-            // The next output tile (grid-stride case) overwrites shared buffer 0.
-            __syncthreads();
-
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int row = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
-                if (row >= m)
-                    continue;
-                float *c_row = c + static_cast<size_t>(row) * n;
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int col = n0 + tx * 4 + 64 * h;
-                    const float2 lo = acc[i][2 * h], hi = acc[i][2 * h + 1];
-                    if (VEC_C && col + 3 < n) {
-                        *reinterpret_cast<float4 *>(c_row + col) = make_float4(lo.x, lo.y, hi.x, hi.y);
-                    } else {
-                        const float v[4] = {lo.x, lo.y, hi.x, hi.y};
-#pragma unroll
-                        for (int q = 0; q < 4; ++q)
-                            if (col + q < n)
-                                c_row[col + q] = v[q];
-                    }
-                }
-            }
-        }
-    }
-}
-
-} // namespace b200
-
-namespace b200 {
-
-// ---------------------------------------------------------------------------
-// Aligned-operand variant: a 3- or 4-stage cp.async pipeline feeds shared memory
-// straight from global memory (no register staging, one barrier per 16- or
-// 32-deep K tile).  A stays row-major in shared memory (rows padded by 4 floats)
-// and is read as float4 along k, so one A fragment load serves four k-slices.
-// Used when A and B rows are 16-byte aligned (k % 4 == 0, n % 4 == 0, aligned bases);
-// partial tiles are zero-filled by cp.async's source-size operand.
-//
 // Split K: a launch with gridDim.z = S > 1 must form clusters of (1, 1, S).  The
 // S CTAs of a cluster compute the same output tile over S consecutive slices of
 // the K tiles, stage their FP32 partial tiles in their own shared memory, and
@@ -218,9 +40,9 @@ namespace b200 {
 // The output tile is BM x BN, each thread owning an RM x RN micro-tile, so the
 // block has (BM/RM) x (BN/RN) threads: 128 x 128 with 8 x 8 per thread (256
 // threads) for large problems and 32 x 32 with 4 x 4 (64 threads) so that
-// smaller outputs still spread over every SM.  A thread's rows are ty, ty + TY, ... (TY = BM/RM): the
-// threads of a warp then read A rows BK + 4 floats apart, which fall in distinct
-// banks.  Its columns come in groups of four, 4*TX apart (TX = BN/RN), so a warp's
+// smaller outputs still spread over every SM.  A thread's rows are ty, ty + TY,
+// ... (TY = BM/RM): the threads of a warp then read A rows BK + 4 floats apart,
+// which fall in distinct banks.  Its columns come in groups of four, 4*TX apart (TX = BN/RN), so a warp's
 // B reads are contiguous 16-byte vectors.
 constexpr int FA_MODEL_BK = 16;                          // K granularity of the launch-plan model
 
@@ -263,6 +85,12 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, bool v
                  : "memory");
 }
 
+// 4-byte copy with zero fill when !valid (unaligned operands).
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void *src, bool valid)
+{
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(valid ? 4 : 0) : "memory");
+}
+
 __device__ __forceinline__ void cp_async_commit()
 {
     asm volatile("cp.async.commit_group;" ::: "memory");
@@ -292,7 +120,7 @@ __device__ __forceinline__ void store_row_vec(float *c_row, int col, int n, cons
     }
 }
 
-template <int BM, int BN, int RM, int RN, bool VEC_C>
+template <int BM, int BN, int RM, int RN, bool VEC_AB, bool VEC_C>
 __global__ void __launch_bounds__(FaTile<BM, BN, RM, RN>::kThreads, FaTile<BM, BN, RM, RN>::kMinBlocks)
 ffma_gemm_async_kernel(const float *__restrict__ a, const float *__restrict__ b, float *__restrict__ c, int m,
                        int n, int k)
@@ -333,9 +161,17 @@ ffma_gemm_async_kernel(const float *__restrict__ a, const float *__restrict__ b,
                     if (T::kAChunks % kThreads == 0 || chunk < T::kAChunks) {
                         const int row = chunk / (BK / 4), kq = chunk % (BK / 4);
                         const int grow = m0 + row, gk = (kt_begin + kt) * BK + kq * 4;
-                        const bool ok = grow < m && gk < k;
-                        const float *src = ok ? a + static_cast<size_t>(grow) * k + gk : a;
-                        cp_async16(as_addr + (s * T::kAStage + row * A_LD + kq * 4) * 4, src, ok);
+                        const uint32_t dst = as_addr + (s * T::kAStage + row * A_LD + kq * 4) * 4;
+                        if constexpr (VEC_AB) {
+                            const bool ok = grow < m && gk < k;
+                            cp_async16(dst, ok ? a + static_cast<size_t>(grow) * k + gk : a, ok);
+                        } else {
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                const bool ok = grow < m && gk + e < k;
+                                cp_async4(dst + 4 * e, ok ? a + static_cast<size_t>(grow) * k + gk + e : a, ok);
+                            }
+                        }
                     }
                 }
 #pragma unroll
@@ -344,9 +180,17 @@ ffma_gemm_async_kernel(const float *__restrict__ a, const float *__restrict__ b,
                     if (T::kBChunks % kThreads == 0 || chunk < T::kBChunks) {
                         const int row = chunk / (BN / 4), cq = chunk % (BN / 4);
                         const int gk = (kt_begin + kt) * BK + row, gcol = n0 + cq * 4;
-                        const bool ok = gk < k && gcol < n;
-                        const float *src = ok ? b + static_cast<size_t>(gk) * n + gcol : b;
-                        cp_async16(bs_addr + (s * T::kBStage + row * BN + cq * 4) * 4, src, ok);
+                        const uint32_t dst = bs_addr + (s * T::kBStage + row * BN + cq * 4) * 4;
+                        if constexpr (VEC_AB) {
+                            const bool ok = gk < k && gcol < n;
+                            cp_async16(dst, ok ? b + static_cast<size_t>(gk) * n + gcol : b, ok);
+                        } else {
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                const bool ok = gk < k && gcol + e < n;
+                                cp_async4(dst + 4 * e, ok ? b + static_cast<size_t>(gk) * n + gcol + e : b, ok);
+                            }
+                        }
                     }
                 }
             };

@@ -180,24 +180,6 @@ cudaError_t launch_pdl_cluster_z(void (*kernel)(Params...), dim3 grid, dim3 bloc
     return cudaLaunchKernelEx(&config, kernel, std::forward<Args>(args)...);
 }
 
-unsigned int pack_grid_x(int64_t cols)
-{
-    const int64_t blocks = (cols + 255) / 256;
-    return static_cast<unsigned int>(blocks < 64 ? (blocks < 1 ? 1 : blocks) : 64);
-}
-
-unsigned int pack_grid_y(int64_t rows)
-{
-    return static_cast<unsigned int>(rows < 4096 ? rows : 4096);
-}
-
-template <typename T, bool ROUND>
-void launch_pack(const void *src, void *dst, int64_t rows, int64_t cols, int64_t ld, cudaStream_t stream)
-{
-    const dim3 grid(pack_grid_x(ld), pack_grid_y(rows));
-    pack_rows_kernel<T, ROUND><<<grid, 256, 0, stream>>>(static_cast<const T *>(src), static_cast<T *>(dst), rows,
-                                                         cols, ld);
-}
 
 // TF32 B: dst (n x ld) = rounded transpose of src (k x n).
 // Both TF32 operands in one launch: rounded A (m x lda) and rounded, transposed B
@@ -228,18 +210,25 @@ cudaError_t prepare_tf32(const Context *ctx, const float *a, float *a_dst, int64
                       stream, prep);
 }
 
-// Prepare one FP16/BF16 operand for TMA (copy with zero padding into scratch).
-void prepare_operand(int prec, const void *src, int64_t rows, int64_t cols, bool direct, void *scratch,
-                     int64_t ld, const Context *ctx, cudaStream_t stream)
+// FP16/BF16 operands TMA cannot read in place, repacked into 16-byte aligned
+// scratch in one launch (an operand with `direct` set is skipped).
+template <typename T>
+cudaError_t pack_operands(const Context *ctx, const void *a, bool a_direct, void *a_dst, int64_t m, int64_t k,
+                          int64_t lda, const void *b, bool b_direct, void *b_dst, int64_t n, int64_t ldb,
+                          cudaStream_t stream)
 {
-    (void)ctx;
-    if (direct)
-        return;
-    if (prec == kPrecBf16) {
-        launch_pack<__nv_bfloat16, false>(src, scratch, rows, cols, ld, stream);
-    } else {
-        launch_pack<__half, false>(src, scratch, rows, cols, ld, stream);
-    }
+    if (a_direct && b_direct)
+        return cudaSuccess;
+    const PackJob<T> ja{static_cast<const T *>(a), static_cast<T *>(a_dst), a_direct ? 0 : m, k, lda};
+    const PackJob<T> jb{static_cast<const T *>(b), static_cast<T *>(b_dst), b_direct ? 0 : k, n, ldb};
+    const int64_t cap = 4LL * ctx->sm_count;
+    auto blocks_for = [&](const PackJob<T> &j) {
+        const int64_t blocks = (j.rows * j.ld + 255) / 256;
+        return blocks < 1 ? int64_t{1} : blocks > cap ? cap : blocks;
+    };
+    const int64_t a_blocks = blocks_for(ja), b_blocks = blocks_for(jb);
+    return launch_pdl(pack_pair_kernel<T>, dim3(static_cast<unsigned int>(a_blocks + b_blocks)), dim3(256), 0,
+                      stream, ja, jb, static_cast<int>(a_blocks));
 }
 
 // tile_n selects the kernel: 0 = CTA pair (256 x 256), else the single-CTA
@@ -488,8 +477,17 @@ int launch_tcgen05(Context *ctx, int prec, const void *a, const void *b, float *
             return fail(error, error_size, "kernel launch", cudaGetErrorString(st));
         }
     } else {
-        prepare_operand(prec, a, m, k, a_direct, const_cast<void *>(a_op), lda, ctx, stream);
-        prepare_operand(prec, b, k, n, b_direct, const_cast<void *>(b_op), ldb, ctx, stream);
+        const cudaError_t st =
+            prec == kPrecBf16
+                ? pack_operands<__nv_bfloat16>(ctx, a, a_direct, const_cast<void *>(a_op), m, k, lda, b, b_direct,
+                                               const_cast<void *>(b_op), n, ldb, stream)
+                : pack_operands<__half>(ctx, a, a_direct, const_cast<void *>(a_op), m, k, lda, b, b_direct,
+                                        const_cast<void *>(b_op), n, ldb, stream);
+        if (st != cudaSuccess) {
+            if (pooled)
+                cudaFreeAsync(pooled, stream);
+            return fail(error, error_size, "kernel launch", cudaGetErrorString(st));
+        }
     }
 
     if (m <= kSkinnyMaxM) {
@@ -569,15 +567,6 @@ int launch_tcgen05(Context *ctx, int prec, const void *a, const void *b, float *
     return 0;
 }
 
-template <bool VA, bool VB, bool VC>
-void launch_ffma_kernel(const float *a, const float *b, float *c, int m, int k, int n, cudaStream_t stream)
-{
-    const int64_t gx = (static_cast<int64_t>(n) + FF_BN - 1) / FF_BN;
-    const int64_t gy = (static_cast<int64_t>(m) + FF_BM - 1) / FF_BM;
-    const dim3 grid(static_cast<unsigned int>(gx < 65535 ? gx : 65535),
-                    static_cast<unsigned int>(gy < 65535 ? gy : 65535));
-    launch_pdl(ffma_gemm_kernel<VA, VB, VC>, grid, dim3(FF_THREADS), 0, stream, a, b, c, m, n, k);
-}
 
 // Launch plan of the aligned FFMA kernel: output tile and K split.  The busiest
 // SM's time is estimated as (its blocks) x (tile area) x (16-deep K steps per
@@ -634,7 +623,7 @@ FfmaPlan choose_ffma_plan(int m, int k, int n, int sm_count, const int *resident
     return best;
 }
 
-template <int BM, int BN, int RM, int RN>
+template <int BM, int BN, int RM, int RN, bool VEC_AB>
 cudaError_t launch_ffma_async(const float *a, const float *b, float *c, int m, int k, int n, int splits, bool vec_c,
                               cudaStream_t stream)
 {
@@ -644,32 +633,30 @@ cudaError_t launch_ffma_async(const float *a, const float *b, float *c, int m, i
     const dim3 grid(static_cast<unsigned int>(gx < 65535 ? gx : 65535),
                     static_cast<unsigned int>(gy < 65535 ? gy : 65535), static_cast<unsigned int>(splits));
     if (vec_c)
-        return launch_pdl_cluster_z(ffma_gemm_async_kernel<BM, BN, RM, RN, true>, grid, dim3(T::kThreads),
+        return launch_pdl_cluster_z(ffma_gemm_async_kernel<BM, BN, RM, RN, VEC_AB, true>, grid, dim3(T::kThreads),
                                     T::kSmemBytes, splits, stream, a, b, c, m, n, k);
-    return launch_pdl_cluster_z(ffma_gemm_async_kernel<BM, BN, RM, RN, false>, grid, dim3(T::kThreads),
+    return launch_pdl_cluster_z(ffma_gemm_async_kernel<BM, BN, RM, RN, VEC_AB, false>, grid, dim3(T::kThreads),
                                 T::kSmemBytes, splits, stream, a, b, c, m, n, k);
+}
+
+template <bool VEC_AB>
+cudaError_t launch_ffma_plan(const FfmaPlan &plan, const float *a, const float *b, float *c, int m, int k, int n,
+                             bool vec_c, cudaStream_t stream)
+{
+    if (plan.tile == 0)
+        return launch_ffma_async<128, 128, 8, 8, VEC_AB>(a, b, c, m, k, n, plan.splits, vec_c, stream);
+    return launch_ffma_async<32, 32, 4, 4, VEC_AB>(a, b, c, m, k, n, plan.splits, vec_c, stream);
 }
 
 int launch_ffma(const Context *ctx, const float *a, const float *b, float *c, int m, int k, int n,
                 cudaStream_t stream, char *error, size_t error_size)
 {
-    const bool va = aligned16(a) && k % 4 == 0;
-    const bool vb = aligned16(b) && n % 4 == 0;
-    const bool vc = aligned16(c) && n % 4 == 0;
-    if (va && vb) {
-        // Aligned operands: cp.async pipeline kernel, tile by the cost model.
-        const FfmaPlan plan = choose_ffma_plan(m, k, n, ctx->sm_count, ctx->ffma_resident);
-        cudaError_t st;
-        switch (plan.tile) {
-        case 0: st = launch_ffma_async<128, 128, 8, 8>(a, b, c, m, k, n, plan.splits, vc, stream); break;
-        default: st = launch_ffma_async<32, 32, 4, 4>(a, b, c, m, k, n, plan.splits, vc, stream); break;
-        }
-        if (st != cudaSuccess)
-            return fail(error, error_size, "kernel launch", cudaGetErrorString(st));
-    } else {
-        launch_ffma_kernel<false, false, false>(a, b, c, m, k, n, stream);
-    }
-    const cudaError_t st = cudaGetLastError();
+    // 16-byte copies when both operands' rows are 16-byte aligned, 4-byte copies otherwise.
+    const bool vec_ab = aligned16(a) && k % 4 == 0 && aligned16(b) && n % 4 == 0;
+    const bool vec_c = aligned16(c) && n % 4 == 0;
+    const FfmaPlan plan = choose_ffma_plan(m, k, n, ctx->sm_count, ctx->ffma_resident);
+    const cudaError_t st = vec_ab ? launch_ffma_plan<true>(plan, a, b, c, m, k, n, vec_c, stream)
+                                  : launch_ffma_plan<false>(plan, a, b, c, m, k, n, vec_c, stream);
     if (st != cudaSuccess)
         return fail(error, error_size, "kernel launch", cudaGetErrorString(st));
     return 0;
@@ -743,14 +730,13 @@ extern "C" int matmul_kernel_info(int implementation, int precision, char *json,
             json, json_size,
             "{\"implementation\":\"ffma\",\"precision\":\"fp32\",\"tile_m\":%d,\"tile_n\":%d,"
             "\"tile_k\":%d,\"threads\":%d,\"warp_tile_m\":%d,\"warp_tile_n\":%d,\"microtile_m\":8,"
-            "\"microtile_n\":8,\"buffering\":%d,\"load_method\":\"cp_async_16B_zero_fill\","
+            "\"microtile_n\":8,\"buffering\":%d,\"load_method\":\"cp_async_zero_fill\","
+            "\"copy_bytes\":\"16 when A and B rows are 16-byte aligned, else 4\","
             "\"tensor_cores\":false,\"fma\":\"ffma2_rn_packed_fp32x2\",\"blocks_per_sm\":2,"
             "\"small_tiles\":[[32,32,4,4]],\"split_k\":\"cluster_1x1xS_dsmem_reduce\","
-            "\"max_splits\":%d,\"plan_choice\":\"cost_model_busiest_sm\","
-            "\"unaligned_kernel\":{\"tile_m\":%d,\"tile_n\":%d,\"tile_k\":%d,\"buffering\":2,"
-            "\"load_method\":\"masked_scalar_register_prefetch\"}}",
+            "\"max_splits\":%d,\"plan_choice\":\"cost_model_busiest_sm\"}",
             FF_BM, FF_BN, FaTile<128, 128, 8, 8>::kBK, FF_THREADS, 16, 128, FaTile<128, 128, 8, 8>::kStages,
-            kFfmaMaxSplits, FF_BM, FF_BN, FF_BK);
+            kFfmaMaxSplits);
     }
     if (written < 0 || static_cast<size_t>(written) >= json_size) {
         json[0] = '\0';
@@ -830,15 +816,15 @@ extern "C" void *matmul_create(int device, char *error, size_t error_size)
             return nullptr;
         }
     }
-#define B200_FFMA_KERNEL(BM, BN, RM, RN)                                                                       \
-    {reinterpret_cast<const void *>(&ffma_gemm_async_kernel<BM, BN, RM, RN, true>),                             \
-     FaTile<BM, BN, RM, RN>::kSmemBytes},                                                                        \
-    {                                                                                                            \
-        reinterpret_cast<const void *>(&ffma_gemm_async_kernel<BM, BN, RM, RN, false>),                          \
-            FaTile<BM, BN, RM, RN>::kSmemBytes                                                                   \
-    }
+#define B200_FFMA_KERNEL(BM, BN, RM, RN, VAB, VC)                                                              \
+    {reinterpret_cast<const void *>(&ffma_gemm_async_kernel<BM, BN, RM, RN, VAB, VC>),                          \
+     FaTile<BM, BN, RM, RN>::kSmemBytes}
+    // Per tile: the (vector A/B, vector C) variant first, whose occupancy the plan uses.
     const std::pair<const void *, int> ffma_kernels[] = {
-        B200_FFMA_KERNEL(128, 128, 8, 8), B200_FFMA_KERNEL(32, 32, 4, 4)};
+        B200_FFMA_KERNEL(128, 128, 8, 8, true, true),  B200_FFMA_KERNEL(128, 128, 8, 8, true, false),
+        B200_FFMA_KERNEL(128, 128, 8, 8, false, true), B200_FFMA_KERNEL(128, 128, 8, 8, false, false),
+        B200_FFMA_KERNEL(32, 32, 4, 4, true, true),    B200_FFMA_KERNEL(32, 32, 4, 4, true, false),
+        B200_FFMA_KERNEL(32, 32, 4, 4, false, true),   B200_FFMA_KERNEL(32, 32, 4, 4, false, false)};
 #undef B200_FFMA_KERNEL
     for (const auto &kernel : ffma_kernels) {
         st = cudaFuncSetAttribute(kernel.first, cudaFuncAttributeMaxDynamicSharedMemorySize, kernel.second);
@@ -848,11 +834,11 @@ extern "C" void *matmul_create(int device, char *error, size_t error_size)
             return nullptr;
         }
     }
-    static_assert(sizeof(ffma_kernels) / sizeof(ffma_kernels[0]) == 2 * kFfmaTileCount, "one pair per tile");
+    static_assert(sizeof(ffma_kernels) / sizeof(ffma_kernels[0]) == 4 * kFfmaTileCount, "four variants per tile");
     for (int t = 0; t < kFfmaTileCount; ++t) {
         const int threads = kFfmaTiles[t].warps * 32;
-        st = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ctx->ffma_resident[t], ffma_kernels[2 * t].first,
-                                                           threads, ffma_kernels[2 * t].second);
+        st = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ctx->ffma_resident[t], ffma_kernels[4 * t].first,
+                                                           threads, ffma_kernels[4 * t].second);
         if (st != cudaSuccess) {
             delete ctx;
             fail_cuda(error, error_size, "cudaOccupancyMaxActiveBlocksPerMultiprocessor", st);
@@ -1012,23 +998,17 @@ extern "C" int matmul_plan(void *opaque, int implementation, int precision, int 
     const Context *ctx = static_cast<const Context *>(opaque);
     int written;
     if (implementation == kImplFfma) {
-        // The aligned kernel runs when A and B rows are 16-byte aligned; bases
-        // are unknown here, so this reports the plan for aligned bases.
-        if (k % 4 == 0 && n % 4 == 0) {
-            const FfmaPlan plan = choose_ffma_plan(m, k, n, ctx->sm_count, ctx->ffma_resident);
-            const FfmaTileOption &o = kFfmaTiles[plan.tile];
-            written = std::snprintf(json, json_size,
-                                    "{\"kernel\":\"ffma_async\",\"tile_m\":%d,\"tile_n\":%d,\"threads\":%d,"
-                                    "\"splits\":%d,\"cluster\":[1,1,%d],\"grid\":[%lld,%lld,%d]}",
-                                    o.bm, o.bn, o.warps * 32, plan.splits, plan.splits,
-                                    static_cast<long long>((n + o.bn - 1) / o.bn),
-                                    static_cast<long long>((m + o.bm - 1) / o.bm), plan.splits);
-        } else {
-            written = std::snprintf(json, json_size,
-                                    "{\"kernel\":\"ffma_generic\",\"tile_m\":%d,\"tile_n\":%d,\"threads\":%d,"
-                                    "\"splits\":1}",
-                                    FF_BM, FF_BN, FF_THREADS);
-        }
+        // One kernel for every alignment; the plan does not depend on the base pointers.
+        const FfmaPlan plan = choose_ffma_plan(m, k, n, ctx->sm_count, ctx->ffma_resident);
+        const FfmaTileOption &o = kFfmaTiles[plan.tile];
+        written = std::snprintf(json, json_size,
+                                "{\"kernel\":\"ffma_async\",\"tile_m\":%d,\"tile_n\":%d,\"threads\":%d,"
+                                "\"splits\":%d,\"cluster\":[1,1,%d],\"grid\":[%lld,%lld,%d],"
+                                "\"vector_loads_if_aligned\":%s}",
+                                o.bm, o.bn, o.warps * 32, plan.splits, plan.splits,
+                                static_cast<long long>((n + o.bn - 1) / o.bn),
+                                static_cast<long long>((m + o.bm - 1) / o.bm), plan.splits,
+                                k % 4 == 0 && n % 4 == 0 ? "true" : "false");
     } else if (m <= kSkinnyMaxM) {
         const int elem = precision == kPrecTf32 ? 4 : 2;
         const int total_k_blocks = static_cast<int>((static_cast<int64_t>(k) + TC_ROW_BYTES / elem - 1) /

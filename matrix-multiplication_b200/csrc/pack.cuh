@@ -5,11 +5,11 @@
 //    src/matmul_custom.cuh:158-164, and of src/precision.py:66-76).  The
 //    tensor core ignores the 13 low fraction bits of a TF32 operand, so inputs
 //    are rounded here first.
-//  * pack_rows: copy a rows x cols row-major matrix with arbitrary (element)
-//    alignment into a 16-byte aligned rows x ld_dst buffer, zero-filling the
-//    padding columns, optionally TF32-rounding.  Used when an FP16/BF16 operand
-//    cannot be described by a TMA tensor map (base not 16-byte aligned, or a row
-//    pitch that is not a multiple of 16 bytes).
+//  * pack_pair: copy rows x cols row-major FP16/BF16 operands with arbitrary
+//    (element) alignment into 16-byte aligned rows x ld buffers, zero-filling the
+//    padding columns -- A and B in one launch.  Used when an operand cannot be
+//    described by a TMA tensor map (base not 16-byte aligned, or a row pitch that
+//    is not a multiple of 16 bytes).
 //  * tf32_prepare: both TF32 operands in one launch -- the rounded A copy and
 //    the rounded, transposed B -- so the GEMM that follows (launched as its
 //    programmatic dependent) overlaps its start-up with this pass.
@@ -37,25 +37,31 @@ __device__ __forceinline__ float round_tf32_rne(float x)
     return __uint_as_float(round_tf32_rne_bits(__float_as_uint(x)));
 }
 
-template <typename T, bool ROUND_TF32>
-__global__ void pack_rows_kernel(const T *__restrict__ src, T *__restrict__ dst, int64_t rows, int64_t cols,
-                                 int64_t ld_dst)
+// One repack job: rows x cols (row-major, element-aligned) -> rows x ld, zero in
+// columns cols..ld-1.  rows == 0 means the operand needs no copy.
+template <typename T>
+struct PackJob {
+    const T *src;
+    T *dst;
+    int64_t rows, cols, ld;
+};
+
+// Both FP16/BF16 operands that TMA cannot read in place, in one launch: blocks
+// [0, a_blocks) copy job a, the rest job b, each a grid-stride loop over the
+// destination's elements (coalesced on both sides).
+template <typename T>
+__global__ void __launch_bounds__(256) pack_pair_kernel(const PackJob<T> a, const PackJob<T> b, int a_blocks)
 {
-    for (int64_t r = blockIdx.y; r < rows; r += gridDim.y) {
-        const T *s = src + r * cols;
-        T *d = dst + r * ld_dst;
-        for (int64_t col = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; col < ld_dst;
-             col += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-            T v;
-            if (col < cols) {
-                v = s[col];
-                if constexpr (ROUND_TF32)
-                    v = round_tf32_rne(v);
-            } else {
-                v = T(0.0f);
-            }
-            d[col] = v;
-        }
+    wait_for_prior_grid();
+    allow_next_grid();
+    const bool first = static_cast<int>(blockIdx.x) < a_blocks;
+    const PackJob<T> job = first ? a : b;
+    const int64_t blocks = first ? a_blocks : static_cast<int64_t>(gridDim.x) - a_blocks;
+    const int64_t block = first ? blockIdx.x : blockIdx.x - a_blocks;
+    const int64_t total = job.rows * job.ld;
+    for (int64_t i = block * 256 + threadIdx.x; i < total; i += blocks * 256) {
+        const int64_t r = i / job.ld, col = i % job.ld;
+        job.dst[i] = col < job.cols ? job.src[r * job.cols + col] : T(0.0f);
     }
 }
 

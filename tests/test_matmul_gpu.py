@@ -204,7 +204,8 @@ def test_ffma_plans_cover_every_tile_and_split(native):
     assert {p["splits"] for p in plans.values()} == {1, 2, 4, 8}
     assert {p["splits"] for p in plans.values() if p["tile_m"] == 128} >= {1, 2, 4}
     assert plans[(32, 144, 32)]["splits"] == 8
-    assert native.plan("ffma", 31, 33, 65)["kernel"] == "ffma_generic"
+    ragged = native.plan("ffma", 31, 33, 65)
+    assert ragged["kernel"] == "ffma_async" and ragged["vector_loads_if_aligned"] is False
 
 
 @pytest.mark.parametrize("shape", FFMA_PLAN_SHAPES)
