@@ -431,6 +431,8 @@ def main() -> int:
     parser.add_argument("--sweep", choices=("square", "llm", "ragged", "all"), default=None,
                         help="instead of the contract line, time every shape of a configuration "
                              "(reference graph method, one JSON line per case, torch/cuBLAS beside it)")
+    parser.add_argument("--cases", nargs="+", default=None, metavar="MxKxN:PREC[:normal]",
+                        help="like --sweep, for the listed shapes (inputs U[-1,1), or N(0, 1/sqrt(K)) with :normal)")
     args = parser.parse_args()
     if args.warmup < 3:
         parser.error("at least 3 warm-up steps")
@@ -441,8 +443,8 @@ def main() -> int:
         args.workload = "square8192" if args.gpus == 1 else "rowshard32768"
     if args.steps is None:
         args.steps = 500 if args.workload == "square8192" else 20
-    if args.sweep:
-        sweep(args.sweep)
+    if args.sweep or args.cases:
+        sweep(args.sweep, [parse_case(text) for text in args.cases] if args.cases else None)
         return 0
     if args.impl == "reference":
         run_reference_arm(args, rank)
@@ -474,7 +476,20 @@ SWEEPS = {
 }
 
 
-def sweep(which: str) -> None:
+def parse_case(text: str) -> tuple:
+    """``"MxKxN:prec"`` or ``"MxKxN:prec:normal"`` -> (m, k, n, prec, distribution)."""
+    parts = text.split(":")
+    if len(parts) not in (2, 3) or parts[1] not in ("fp32", "tf32", "fp16", "bf16") or \
+            (len(parts) == 3 and parts[2] not in ("normal", "uniform")):
+        raise SystemExit(f"bad case {text!r}: use MxKxN:fp32|tf32|fp16|bf16[:normal]")
+    dims = parts[0].lower().split("x")
+    if len(dims) != 3 or not all(d.isdigit() and int(d) > 0 for d in dims):
+        raise SystemExit(f"bad case {text!r}: the shape is MxKxN with positive sizes")
+    m, k, n = (int(d) for d in dims)
+    return m, k, n, parts[1], parts[2] if len(parts) == 3 else "uniform"
+
+
+def sweep(which: str | None, explicit: list | None = None) -> None:
     """Time each case with the reference's CUDA-graph method; print one JSON line per case."""
     import torch
 
@@ -482,7 +497,8 @@ def sweep(which: str) -> None:
     from precision import INPUT_DTYPES, torch_precision
 
     peaks, _ = load_peaks()
-    cases = [c for key in (("square", "llm", "ragged") if which == "all" else (which,)) for c in SWEEPS[key]]
+    cases = explicit if explicit is not None else \
+        [c for key in (("square", "llm", "ragged") if which == "all" else (which,)) for c in SWEEPS[key]]
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
     native = NativeMatmul(device=0)
