@@ -97,6 +97,15 @@ int matmul_check_fp64(void *context, int precision, const void *a, const void *b
 int matmul_plan(void *context, int implementation, int precision, int m, int k, int n, char *json,
                 size_t json_size, char *error, size_t error_size);
 
+/* No counterpart in the reference.  Limits the tensor-core launches of this
+ * context to `sms` SMs (0 = the whole device): persistent grids, CTA pairs and
+ * split-K clusters are sized for the limit and the launch plan assumes it.  For
+ * running a GEMM next to communication kernels that need SMs of their own (the
+ * row-sharded multi-GPU GEMM overlaps its NCCL exchanges this way).  FP32 FFMA
+ * grids are not limited.  Takes effect for later launches; not synchronised with
+ * launches from other threads on the same context. */
+int matmul_set_sm_limit(void *context, int sms, char *error, size_t error_size);
+
 /* No counterpart in the reference.  Same arguments, result and error convention
  * as matmul_launch, for implementation 7 (tcgen05) only, but it never allocates:
  * for callers that must not call cudaMalloc or a stream-ordered allocator --

@@ -74,9 +74,14 @@ struct Context {
     int device = 0;
     int major = 0;
     int minor = 0;
+    // What the tensor-core launches may use: the device's SMs, or fewer after
+    // matmul_set_sm_limit (the device_* fields keep the device's own values).
     int sm_count = 0;
     int max_pairs = 0;        // co-resident 2-CTA clusters of the pair kernel
     int max_split_ctas[4] = {}; // co-resident CTAs of the single-CTA kernel in (1,1,S) clusters, S = 1,2,4,8
+    int device_sm_count = 0;
+    int device_max_pairs = 0;
+    int device_max_split_ctas[4] = {};
     int ffma_resident[2] = {}; // resident blocks per SM of each aligned FFMA tile
     EncodeTiledFn encode = nullptr;
     cudaMemPool_t pool = nullptr;
@@ -919,6 +924,10 @@ extern "C" void *matmul_create(int device, char *error, size_t error_size)
         }
         ctx->max_split_ctas[i] = clusters * static_cast<int>(size);
     }
+    ctx->device_sm_count = ctx->sm_count;
+    ctx->device_max_pairs = ctx->max_pairs;
+    for (int i = 0; i < 4; ++i)
+        ctx->device_max_split_ctas[i] = ctx->max_split_ctas[i];
 
     cudaMemPoolProps props{};
     props.allocType = cudaMemAllocationTypePinned;
@@ -1018,19 +1027,45 @@ extern "C" int matmul_plan(void *opaque, int implementation, int precision, int 
                                 m <= 16 ? 16 : m <= 32 ? 32 : 64, SK_BM, skinny_splits(ctx, n, total_k_blocks));
     } else {
         const TcPlan plan = choose_tc_plan(ctx, m, k, n, precision);
+        const int64_t tiles =
+            plan.tile_n == 0
+                ? ((static_cast<int64_t>(m) + TC2_BM - 1) / TC2_BM) * ((static_cast<int64_t>(n) + TC2_BN - 1) / TC2_BN)
+                : ((static_cast<int64_t>(m) + TC_BM - 1) / TC_BM) *
+                      ((static_cast<int64_t>(n) + plan.tile_n - 1) / plan.tile_n);
+        const int64_t ctas = plan.tile_n == 0 ? 2 * (tiles < ctx->max_pairs ? tiles : ctx->max_pairs)
+                             : plan.splits > 1 ? tiles * plan.splits
+                                               : (tiles < ctx->sm_count ? tiles : ctx->sm_count);
         written = plan.tile_n == 0
                       ? std::snprintf(json, json_size,
                                       "{\"kernel\":\"tc2_pair\",\"tile_m\":%d,\"tile_n\":%d,\"cluster\":[2,1,1],"
-                                      "\"splits\":1}",
-                                      TC2_BM, TC2_BN)
+                                      "\"splits\":1,\"ctas\":%lld}",
+                                      TC2_BM, TC2_BN, static_cast<long long>(ctas))
                       : std::snprintf(json, json_size,
                                       "{\"kernel\":\"tc_single\",\"tile_m\":%d,\"tile_n\":%d,\"splits\":%d,"
-                                      "\"cluster\":[1,1,%d]}",
-                                      TC_BM, plan.tile_n, plan.splits, plan.splits);
+                                      "\"cluster\":[1,1,%d],\"ctas\":%lld}",
+                                      TC_BM, plan.tile_n, plan.splits, plan.splits, static_cast<long long>(ctas));
     }
     if (written < 0 || static_cast<size_t>(written) >= json_size) {
         json[0] = '\0';
         return fail(error, error_size, "matmul_plan", "JSON buffer too small");
+    }
+    return 0;
+}
+
+extern "C" int matmul_set_sm_limit(void *opaque, int sms, char *error, size_t error_size)
+{
+    clear_error(error, error_size);
+    if (!opaque)
+        return fail(error, error_size, "matmul_set_sm_limit", "context is null");
+    Context *ctx = static_cast<Context *>(opaque);
+    if (sms < 0 || (sms > 0 && sms < 2))
+        return fail(error, error_size, "matmul_set_sm_limit", "the limit must be 0 (no limit) or at least 2 SMs");
+    const int limit = sms == 0 || sms > ctx->device_sm_count ? ctx->device_sm_count : sms;
+    ctx->sm_count = limit;
+    ctx->max_pairs = ctx->device_max_pairs < limit / 2 ? ctx->device_max_pairs : limit / 2;
+    for (int i = 0; i < 4; ++i) {
+        const int whole = limit / (1 << i) * (1 << i);
+        ctx->max_split_ctas[i] = ctx->device_max_split_ctas[i] < whole ? ctx->device_max_split_ctas[i] : whole;
     }
     return 0;
 }

@@ -164,6 +164,16 @@ class NativeMatmul:
             raise RuntimeError(self._error_message("matmul_plan", error))
         return json.loads(result.value)
 
+    def set_sm_limit(self, sms: int) -> None:
+        """Run later tensor-core launches on at most ``sms`` SMs (0 = all of them)."""
+        if self._context is None:
+            raise RuntimeError("NativeMatmul context is closed")
+        if isinstance(sms, bool) or not isinstance(sms, int):
+            raise TypeError("sms must be an int")
+        error = ctypes.create_string_buffer(_ERROR_SIZE)
+        if self._library.matmul_set_sm_limit(self._context, sms, error, len(error)) != 0:
+            raise RuntimeError(self._error_message("matmul_set_sm_limit", error))
+
     def convert(self, src: torch.Tensor, dst: torch.Tensor, precision: str) -> torch.Tensor:
         """Convert FP32 ``src`` into ``dst`` (the input dtype of ``precision``) on the device.
 
@@ -256,6 +266,8 @@ def _bind(library) -> None:
         ctypes.c_char_p, ctypes.c_size_t, ctypes.c_char_p, ctypes.c_size_t,
     ]
     library.matmul_plan.restype = ctypes.c_int
+    library.matmul_set_sm_limit.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_char_p, ctypes.c_size_t]
+    library.matmul_set_sm_limit.restype = ctypes.c_int
 
 
 def kernel_info(library, implementation: str, precision: str) -> dict:

@@ -9,7 +9,11 @@ The reference is single-device (src/benchmark_backends.py selects one
   chunk at a time, and every finished chunk is exchanged with grouped
   point-to-point transfers straight into each peer's full C (all-gather) or
   into rank 0's C only (gather to root), so the exchange of chunk i overlaps
-  the GEMM of chunk i+1.  No kernel reads peer memory.
+  the GEMM of chunk i+1.  No kernel reads peer memory;
+* with ``BroadcastPipeline`` the B broadcast runs on its own communicator one
+  step ahead (double-buffered B), so it too overlaps the GEMMs; the GEMMs are
+  then launched on fewer SMs than the device has (``matmul_set_sm_limit``) so
+  that the communication kernels find free SMs while they run.
 
 Collectives are issued through ``torch.distributed`` (one process per GPU);
 the host-side plan (row ranges, chunking, peer lists) is independent of the
@@ -118,3 +122,54 @@ def sharded_step(plan: ShardPlan, a_local: torch.Tensor, b: torch.Tensor, c_full
     for work in works:
         work.wait()
 
+
+
+class BroadcastPipeline:
+    """Double-buffered B whose broadcast for the next step overlaps this step's work.
+
+    ``current`` holds the B every rank computes with now; ``start()`` broadcasts
+    rank 0's ``pending`` buffer (the next step's B) into every rank's ``pending``
+    on the communicator ``group`` without blocking the compute stream, and
+    ``finish()`` makes the current stream wait for it and swaps the buffers.
+    Every step still moves one full B from rank 0 to all ranks.
+    """
+
+    def __init__(self, b: torch.Tensor, group=None):
+        self.current = b
+        self.pending = b.clone()          # rank 0: the next step's B (the same matrix here)
+        self.group = group
+        self.work = None
+
+    def start(self) -> None:
+        if self.work is not None:
+            raise RuntimeError("broadcast already in flight")
+        self.work = dist.broadcast(self.pending, src=0, group=self.group, async_op=True)
+
+    def finish(self) -> None:
+        if self.work is None:
+            raise RuntimeError("no broadcast in flight")
+        self.work.wait()
+        self.work = None
+        self.current, self.pending = self.pending, self.current
+
+
+def pipelined_step(plan: ShardPlan, a_local: torch.Tensor, pipe: BroadcastPipeline, c_full: torch.Tensor,
+                   gemm: Callable[[torch.Tensor, torch.Tensor, torch.Tensor], None], group=None) -> None:
+    """``sharded_step`` with the B broadcast for the next step overlapping this one.
+
+    Every rank posts the broadcast of the next B, runs its chunked GEMMs on the
+    current B with the C exchange of each chunk, and ends the step when both the
+    exchanges and the broadcast are complete.
+    """
+    if plan.world > 1:
+        pipe.start()
+    start, _ = plan.local_rows
+    works = []
+    for index, (lo, hi) in enumerate(plan.chunk_ranges[plan.rank]):
+        gemm(a_local[lo:hi], pipe.current, c_full[start + lo:start + hi])
+        if plan.world > 1:
+            works.extend(exchange_chunk(plan, index, c_full, group))
+    for work in works:
+        work.wait()
+    if plan.world > 1:
+        pipe.finish()

@@ -1,6 +1,7 @@
 """Host logic of the row-sharded multi-GPU GEMM on CPU ranks (gloo, world size 2
-and 3): row plans, the B broadcast and the chunked all-gather / gather-to-root
-exchange, with an FP32 torch product standing in for the GPU kernel."""
+and 3): row plans, the B broadcast (blocking, or pipelined one step ahead on its
+own communicator) and the chunked all-gather / gather-to-root exchange, with an
+FP32 torch product standing in for the GPU kernel."""
 
 from __future__ import annotations
 
@@ -12,7 +13,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from sharded import ShardPlan, chunk_rows, shard_rows, sharded_step
+from sharded import BroadcastPipeline, ShardPlan, chunk_rows, pipelined_step, shard_rows, sharded_step
 
 
 def test_shard_rows_partition_every_row_once():
@@ -54,11 +55,14 @@ def _cpu_gemm(a_rows, b, c_rows):
     torch.matmul(a_rows, b, out=c_rows)
 
 
-def _worker(rank, world, port, m, k, n, chunks, gather, results):
+def _worker(rank, world, port, m, k, n, chunks, gather, results, pipelined=False):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
+        if pipelined:
+            _pipelined(rank, world, m, k, n, chunks, gather, results)
+            return
         torch.manual_seed(0)
         a_full = torch.randn(m, k)
         b_full = torch.randn(k, n)
@@ -80,14 +84,40 @@ def _worker(rank, world, port, m, k, n, chunks, gather, results):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,m,chunks,gather", [(2, 64, 4, "all"), (2, 37, 3, "all"), (3, 50, 2, "root"),
-                                                    (2, 5, 8, "root")])
-def test_row_sharded_gemm_on_gloo_ranks(world, m, chunks, gather):
+def _pipelined(rank, world, m, k, n, chunks, gather, results):
+    """Three steps whose B changes every step: step s must compute with B_s."""
+    b_group = dist.new_group(list(range(world)))
+    torch.manual_seed(0)
+    a_full = torch.randn(m, k)
+    bs = [torch.randn(k, n) for _ in range(4)]
+    plan = ShardPlan(m, k, n, world, rank, chunks=chunks, gather=gather)
+    start, stop = plan.local_rows
+    a_local = a_full[start:stop].clone()
+    b0 = bs[0].clone() if rank == 0 else torch.zeros(k, n)
+    dist.broadcast(b0, src=0)                        # B of the first step, before the loop
+    pipe = BroadcastPipeline(b0, b_group)
+    ok = True
+    for step in range(3):
+        if rank == 0:
+            pipe.pending.copy_(bs[step + 1])         # rank 0 supplies the next step's B
+        c = torch.full((m, n), float("nan"))
+        pipelined_step(plan, a_local, pipe, c, _cpu_gemm)
+        expected = a_full @ bs[step]
+        rows = slice(None) if gather == "all" or rank == 0 else slice(start, stop)
+        ok = ok and torch.allclose(c[rows], expected[rows], rtol=1e-5, atol=1e-4)
+        ok = ok and torch.equal(pipe.current, bs[step + 1])
+    results[rank] = bool(ok)
+
+
+@pytest.mark.parametrize("world,m,chunks,gather,pipelined", [
+    (2, 64, 4, "all", False), (2, 37, 3, "all", False), (3, 50, 2, "root", False), (2, 5, 8, "root", False),
+    (2, 64, 4, "all", True), (3, 50, 2, "root", True)])
+def test_row_sharded_gemm_on_gloo_ranks(world, m, chunks, gather, pipelined):
     ctx = mp.get_context("spawn")
     manager = ctx.Manager()
     results = manager.dict()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, m, 24, 40, chunks, gather, results))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, m, 24, 40, chunks, gather, results, pipelined))
              for r in range(world)]
     for p in procs:
         p.start()
