@@ -15,8 +15,11 @@ Metric: device-timed TFLOP/s = 2*M*K*N / t (the reference's src/main.py:102).
   src/benchmark_backends.py:49-69) for every precision and torch/cuBLAS on the
   same inputs.
 * N > 1 (default workload ``rowshard32768``): M=K=N=32768 BF16, U[-1,1), A and C
-  row-sharded over the ranks, B broadcast from rank 0, C all-gathered; one
-  process per GPU under torchrun; time = max over ranks.
+  row-sharded over the ranks; every step broadcasts one B from rank 0 (posted
+  one step ahead on its own communicator, overlapping the GEMMs) and
+  all-gathers C in row chunks that overlap the next chunk's GEMM, with
+  ``--reserve-sms`` SMs left to the NCCL kernels; one process per GPU under
+  torchrun; time = max over ranks.
 * ``--impl reference`` times the reference's CPU path (numpy FP32 GEMM,
   src/benchmark_backends.py:223-226) on the host cores over row slabs of the
   same workload; under torchrun only rank 0 runs it.
@@ -346,11 +349,12 @@ def multi_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
     import torch.distributed as dist
 
     from gpumat import NativeMatmul
-    from sharded import ShardPlan, sharded_step
+    from sharded import BroadcastPipeline, ShardPlan, pipelined_step
 
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    b_group = dist.new_group(list(range(world)))       # B broadcasts on their own communicator
     size = args.size or 32768
     m = k = n = size
     plan = ShardPlan(m, k, n, world, rank, chunks=args.chunks, gather=args.gather)
@@ -370,16 +374,25 @@ def multi_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
         native.convert(b32, b, "bf16")
         del b32
     c = torch.empty((m, n), dtype=torch.float32, device=device)
+    dist.broadcast(b, src=0)                            # the first step's B, before the loop
+    pipe = BroadcastPipeline(b, b_group)
+    del b
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    if args.reserve_sms:
+        native.set_sm_limit(max(2, sms - args.reserve_sms))
     runs = {}
 
     def gemm(a_rows, b_full, c_rows):
-        key = (a_rows.data_ptr(), c_rows.data_ptr())
+        key = (a_rows.data_ptr(), b_full.data_ptr(), c_rows.data_ptr())
         if key not in runs:
             runs[key] = native.prepare("tcgen05", a_rows, b_full, c_rows, precision="bf16")
         runs[key]()
 
+    def step():
+        pipelined_step(plan, a, pipe, c, gemm)
+
     for _ in range(args.warmup):
-        sharded_step(plan, a, b, c, gemm)
+        step()
     dist.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -387,7 +400,7 @@ def multi_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
         wall0 = time.time()
         e0.record(stream)
         for _ in range(args.steps):
-            sharded_step(plan, a, b, c, gemm)
+            step()
         e1.record(stream)
         torch.cuda.synchronize()
         wall1 = time.time()
@@ -408,9 +421,12 @@ def multi_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic: U[-1,1) from fixed seeds, rounded to BF16",
         "config": {"workload": f"rowshard_bf16_{m}x{k}x{n}", "m": m, "k": k, "n": n, "precision": "bf16",
-                   "parallelism": f"row-sharded A/C over {world} ranks, B broadcast, C "
-                                  f"{'all-gathered' if args.gather == 'all' else 'gathered to rank 0'}",
-                   "chunks": plan.chunk_count, "l2": "inputs larger than L2"},
+                   "parallelism": f"row-sharded A/C over {world} ranks; every step broadcasts one B (NCCL, own "
+                                  f"communicator, posted one step ahead and overlapping the GEMMs) and "
+                                  f"{'all-gathers' if args.gather == 'all' else 'gathers to rank 0'} C in row "
+                                  f"chunks overlapping the next chunk's GEMM",
+                   "chunks": plan.chunk_count, "gemm_sms": sms - args.reserve_sms if args.reserve_sms else sms,
+                   "l2": "inputs larger than L2"},
         "gpu_launches": args.steps * plan.chunk_count,
         "clocks": clock_summary, "device_status": status,
     }
@@ -425,7 +441,9 @@ def main() -> int:
     parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
     parser.add_argument("--workload", choices=("square8192", "rowshard32768"), default=None)
     parser.add_argument("--size", type=int, default=None, help="override the sharded problem size")
-    parser.add_argument("--chunks", type=int, default=4)
+    parser.add_argument("--chunks", type=int, default=8)
+    parser.add_argument("--reserve-sms", type=int, default=16,
+                        help="multi-GPU: SMs left free of GEMM CTAs for the NCCL kernels that overlap them")
     parser.add_argument("--gather", choices=("all", "root"), default="all")
     parser.add_argument("--quick", action="store_true", help="skip the per-precision and cuBLAS tables")
     parser.add_argument("--sweep", choices=("square", "llm", "ragged", "all"), default=None,
