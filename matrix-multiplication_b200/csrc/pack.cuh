@@ -95,16 +95,26 @@ __global__ void __launch_bounds__(256) tf32_prepare_kernel(const Tf32Prep p)
     if (static_cast<int>(blockIdx.x) < p.a_blocks) {
         const int64_t stride = static_cast<int64_t>(p.a_blocks) * 256;
         if (p.a_vec) {
+            // Four independent 16-byte loads in flight per thread per iteration.
             const float4 *src = reinterpret_cast<const float4 *>(p.a);
             float4 *dst = reinterpret_cast<float4 *>(p.a_dst);
             const int64_t count4 = p.m * p.k / 4;
-            for (int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + tid; i < count4; i += stride) {
-                float4 v = src[i];
-                v.x = round_tf32_rne(v.x);
-                v.y = round_tf32_rne(v.y);
-                v.z = round_tf32_rne(v.z);
-                v.w = round_tf32_rne(v.w);
-                dst[i] = v;
+            for (int64_t base = static_cast<int64_t>(blockIdx.x) * 256 + tid; base < count4; base += 4 * stride) {
+                float4 v[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    if (base + u * stride < count4)
+                        v[u] = src[base + u * stride];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    if (base + u * stride < count4) {
+                        v[u].x = round_tf32_rne(v[u].x);
+                        v[u].y = round_tf32_rne(v[u].y);
+                        v[u].z = round_tf32_rne(v[u].z);
+                        v[u].w = round_tf32_rne(v[u].w);
+                        dst[base + u * stride] = v[u];
+                    }
+                }
             }
         } else {
             const int64_t total = p.m * p.lda;
