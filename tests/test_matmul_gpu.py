@@ -169,6 +169,23 @@ def test_tcgen05_split_k_against_fp64_oracle(native, precision, shape):
     _run_and_verify(native, "tcgen05", precision, a_np, b_np, offset=False)
 
 
+def test_sm_limit_bounds_the_launch_and_keeps_results(native):
+    m, k, n = 2048, 1024, 3072
+    full = native.plan("tcgen05", m, k, n, precision="bf16")
+    a_np = po.seeded_uniform((m, k), 21)
+    b_np = po.seeded_uniform((k, n), 22)
+    try:
+        native.set_sm_limit(40)
+        limited = native.plan("tcgen05", m, k, n, precision="bf16")
+        assert limited["ctas"] <= 40 < full["ctas"]
+        _run_and_verify(native, "tcgen05", "bf16", a_np, b_np, offset=False, runs=1)
+        with pytest.raises(RuntimeError):
+            native.set_sm_limit(1)
+    finally:
+        native.set_sm_limit(0)
+    assert native.plan("tcgen05", m, k, n, precision="bf16") == full
+
+
 def test_tcgen05_split_k_is_deterministic_and_graph_capturable(native):
     m, k, n = 512, 8192, 512
     assert native.plan("tcgen05", m, k, n, precision="bf16")["splits"] > 1
