@@ -573,22 +573,22 @@ int launch_tcgen05(Context *ctx, int prec, const void *a, const void *b, float *
 }
 
 
-// Launch plan of the aligned FFMA kernel: output tile and K split.  The busiest
-// SM's time is estimated as (its blocks) x (tile area) x (16-deep K steps per
-// split) / efficiency, where efficiency falls when fewer than about 14 warps are
-// resident and the 32 x 32 tile's 4 x 4 micro-tile is 25 % less efficient than
-// the 8 x 8 one; plus, per wave of resident blocks, a pipeline fill and epilogue
-// worth two K steps and, when split, a reduction worth one.  Fitted to measured
-// B200 times of every tile and split over square sizes 64-4096 and skinny /
-// long-K shapes (the chosen plan is within 3 % of the fastest on average, 14 %
-// at worst).  128 x 64 and 64 x 64 tiles were measured too and never won by
-// enough to keep.
+// Launch plan of the FFMA kernel: output tile and K split.  The busiest SM's
+// time is estimated as (its blocks) x (tile area) x (16-deep K steps per split) /
+// efficiency, where efficiency falls when fewer than about 17 warps are resident
+// (0.3 + warps / 24) and the 32 x 32 tile's 4 x 4 micro-tile is 40 % less
+// efficient than the 8 x 8 one; plus, per wave of resident blocks, a pipeline
+// fill and epilogue worth two K steps and, when split, the cluster exchange worth
+// eight.  Fitted to measured B200 times of every tile and split over square sizes
+// 64-4096, skinny / long-K and ragged (unaligned, short-K) shapes: the chosen
+// plan is within 2.4 % of the fastest on average, 14 % at worst.  128 x 64 and
+// 64 x 64 tiles were measured too and never won by enough to keep.
 struct FfmaTileOption {
     int bm, bn, warps, bk;
     double efficiency;
 };
 constexpr FfmaTileOption kFfmaTiles[] = {{128, 128, 8, FaTile<128, 128, 8, 8>::kBK, 1.0},
-                                         {32, 32, 2, FaTile<32, 32, 4, 4>::kBK, 0.75}};
+                                         {32, 32, 2, FaTile<32, 32, 4, 4>::kBK, 0.6}};
 constexpr int kFfmaTileCount = sizeof(kFfmaTiles) / sizeof(kFfmaTiles[0]);
 constexpr int kFfmaMaxSplits = 8;                       // portable cluster size
 
@@ -614,11 +614,11 @@ FfmaPlan choose_ffma_plan(int m, int k, int n, int sm_count, const int *resident
             const int64_t concurrent = per_sm < slots ? per_sm : slots;
             const int64_t waves = (per_sm + slots - 1) / slots;
             const int64_t kt = (total_kt + splits - 1) / splits;
-            const double occupancy = 0.4 + static_cast<double>(concurrent * o.warps) / 24.0;
+            const double occupancy = 0.3 + static_cast<double>(concurrent * o.warps) / 24.0;
             const double efficiency = o.efficiency * (occupancy < 1.0 ? occupancy : 1.0);
             const double area = static_cast<double>(o.bm) * o.bn;
             const double cost = static_cast<double>(per_sm) * area * static_cast<double>(kt) / efficiency +
-                                (splits > 1 ? 3.0 : 2.0) * static_cast<double>(waves * concurrent) * area;
+                                (splits > 1 ? 8.0 : 2.0) * static_cast<double>(waves * concurrent) * area;
             if ((t == 0 && splits == 1) || cost < best_cost * 0.999) {
                 best = {t, splits};
                 best_cost = cost;

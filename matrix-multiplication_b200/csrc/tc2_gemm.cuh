@@ -232,7 +232,6 @@ tc2_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
             }
             tc_fence_after();
             const int tile_row0 = mb * TC2_BM + static_cast<int>(rank) * TC2_HALF;   // first row of this CTA's part of the tile
-            const int row0 = tile_row0 + quarter * 32;
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                    static_cast<uint32_t>(acc * TC2_BN);
 #pragma unroll 1
@@ -270,14 +269,26 @@ tc2_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
                     }
                     ++stores;
                 } else {
-                    const int row = row0 + lane;
-                    if (row < p.m) {
-                        float *dst = p.c + static_cast<size_t>(row) * p.n;
+                    // C is not TMA-compatible: the same shared-memory box, written out one
+                    // row per warp instruction (lane = column) with bounds-checked stores.
+                    const uint32_t box = s_epi + (stores & 1u) * (4 * TC_EPI_BOX);
+                    epilogue_sync();
+                    const int r = quarter * 32 + lane;
+                    const uint32_t row_addr = box + r * 128;
 #pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            if (col0 + j < p.n)
-                                dst[col0 + j] = __uint_as_float(v[j]);
+                    for (int j = 0; j < 8; ++j)
+                        st_shared_v4(row_addr + ((j ^ (r & 7)) << 4), v[4 * j], v[4 * j + 1], v[4 * j + 2],
+                                     v[4 * j + 3]);
+                    epilogue_sync();
+                    const float *box_f = reinterpret_cast<const float *>(smem_raw + (box - raw));
+                    const int gcol = col0 + lane;
+                    for (int rr = quarter; rr < TC_BM; rr += 4) {
+                        const int grow = tile_row0 + rr;
+                        if (grow < p.m && gcol < p.n)
+                            p.c[static_cast<size_t>(grow) * p.n + gcol] =
+                                box_f[rr * 32 + (((lane >> 2) ^ (rr & 7)) << 2) + (lane & 3)];
                     }
+                    ++stores;
                 }
             }
             if (++acc == 2) {

@@ -211,7 +211,8 @@ def test_tcgen05_split_k_is_deterministic_and_graph_capturable(native):
 # (32 x 144 x 32: 9 K tiles over 8 CTAs).
 FFMA_PLAN_SHAPES = ((64, 64, 64), (128, 128, 128), (32, 144, 32), (100, 3000, 200), (384, 2048, 640),
                     (768, 768, 768), (1024, 64, 1024), (1536, 256, 1536), (1024, 1024, 1024),
-                    (640, 1024, 832), (2048, 512, 2048), (1200, 64, 2400), (260, 2052, 196))
+                    (640, 1024, 832), (2048, 512, 2048), (1200, 64, 2400), (260, 2052, 196),
+                    (1408, 512, 1408), (512, 2048, 896))
 
 
 def test_ffma_plans_cover_every_tile_and_split(native):
