@@ -54,7 +54,10 @@ int matmul_destroy(void *context, char *error, size_t error_size);
 /* Replaces matmul_launch (src/matmul.cu:349-479): C = A * B on `stream`
  * (a cudaStream_t), asynchronous, CUDA-graph capturable.  TF32 inputs are
  * rounded to nearest-even before the tensor-core product; unaligned or
- * TMA-incompatible operands are repacked into stream-ordered scratch first. */
+ * TMA-incompatible operands are repacked into stream-ordered scratch first.
+ * TF32 problems with m*k*n <= 2^25 run on the FFMA kernel with each K tile of
+ * the operands rounded to TF32 (nearest even) in shared memory: the same exact
+ * products, accumulated in FP32, without the operand pre-pass. */
 int matmul_launch(void *context, int implementation, int precision,
                   const void *a, const void *b, float *c, int m, int k, int n,
                   void *stream, char *error, size_t error_size);

@@ -21,6 +21,7 @@
 
 #include <cstdint>
 
+#include "pack.cuh"
 #include "ptx.cuh"
 
 namespace b200 {
@@ -120,7 +121,11 @@ __device__ __forceinline__ void store_row_vec(float *c_row, int col, int n, cons
     }
 }
 
-template <int BM, int BN, int RM, int RN, bool VEC_AB, bool VEC_C>
+// TF32_ROUND: each K tile is rounded to TF32 (nearest even) in shared memory once
+// it has landed -- the TF32 GEMM of small problems on the FFMA pipe: a product of
+// two TF32 values is exact in FP32, so the result has the same products as the
+// tensor-core path, accumulated in FP32.
+template <int BM, int BN, int RM, int RN, bool VEC_AB, bool VEC_C, bool TF32_ROUND = false>
 __global__ void __launch_bounds__(FaTile<BM, BN, RM, RN>::kThreads, FaTile<BM, BN, RM, RN>::kMinBlocks)
 ffma_gemm_async_kernel(const float *__restrict__ a, const float *__restrict__ b, float *__restrict__ c, int m,
                        int n, int k)
@@ -218,12 +223,28 @@ ffma_gemm_async_kernel(const float *__restrict__ a, const float *__restrict__ b,
                 cp_async_commit();
                 const float *at = as + (kt % STAGES) * T::kAStage;
                 const float *bt = bs + (kt % STAGES) * T::kBStage;
+                if constexpr (TF32_ROUND) {
+                    // Round this stage in place once (every value is read by several threads).
+                    float4 *stage_a = reinterpret_cast<float4 *>(as + (kt % STAGES) * T::kAStage);
+                    float4 *stage_b = reinterpret_cast<float4 *>(bs + (kt % STAGES) * T::kBStage);
+                    for (int i = tid; i < T::kAStage / 4 + T::kBStage / 4; i += kThreads) {
+                        float4 *q = i < T::kAStage / 4 ? stage_a + i : stage_b + (i - T::kAStage / 4);
+                        float4 v = *q;
+                        v.x = round_tf32_rne(v.x);
+                        v.y = round_tf32_rne(v.y);
+                        v.z = round_tf32_rne(v.z);
+                        v.w = round_tf32_rne(v.w);
+                        *q = v;
+                    }
+                    __syncthreads();
+                }
 #pragma unroll
                 for (int k4 = 0; k4 < BK; k4 += 4) {
                     float4 ar[RM];
 #pragma unroll
                     for (int i = 0; i < RM; ++i)
                         ar[i] = *reinterpret_cast<const float4 *>(at + T::row(ty, i) * A_LD + k4);
+
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
                         float2 bp[RN / 2];

@@ -436,10 +436,17 @@ int launch_skinny(Context *ctx, int prec, const void *a_op, int64_t lda, const v
     return 0;
 }
 
+bool tf32_on_ffma(int m, int k, int n);
+int launch_ffma_tf32(const Context *ctx, const float *a, const float *b, float *c, int m, int k, int n,
+                     cudaStream_t stream, char *error, size_t error_size);
+
 int launch_tcgen05(Context *ctx, int prec, const void *a, const void *b, float *c, int m, int k, int n,
                    cudaStream_t stream, char *error, size_t error_size, void *fixed_scratch = nullptr,
                    size_t fixed_scratch_bytes = 0)
 {
+    if (prec == kPrecTf32 && tf32_on_ffma(m, k, n))
+        return launch_ffma_tf32(ctx, static_cast<const float *>(a), static_cast<const float *>(b), c, m, k, n,
+                                stream, error, error_size);
     const int elem = prec == kPrecTf32 ? 4 : 2;
     const int64_t align_elems = 16 / elem;
     // TMA needs 16-byte aligned bases and row pitches; TF32 always needs rounding.
@@ -597,13 +604,16 @@ struct FfmaPlan {
     int splits;
 };
 
-FfmaPlan choose_ffma_plan(int m, int k, int n, int sm_count, const int *resident)
+FfmaPlan choose_ffma_plan(int m, int k, int n, int sm_count, const int *resident, unsigned tiles_allowed = 3u)
 {
     FfmaPlan best{0, 1};
     double best_cost = 0.0;
     // Work in 16-deep K units; a split never has fewer K tiles of its own depth than one.
     const int64_t total_kt = (static_cast<int64_t>(k) + FA_MODEL_BK - 1) / FA_MODEL_BK;
+    bool have = false;
     for (int t = 0; t < kFfmaTileCount; ++t) {
+        if (!((tiles_allowed >> t) & 1u))
+            continue;
         const FfmaTileOption &o = kFfmaTiles[t];
         const int64_t tile_kt = (static_cast<int64_t>(k) + o.bk - 1) / o.bk;
         const int64_t tiles = ((static_cast<int64_t>(m) + o.bm - 1) / o.bm) *
@@ -619,16 +629,17 @@ FfmaPlan choose_ffma_plan(int m, int k, int n, int sm_count, const int *resident
             const double area = static_cast<double>(o.bm) * o.bn;
             const double cost = static_cast<double>(per_sm) * area * static_cast<double>(kt) / efficiency +
                                 (splits > 1 ? 8.0 : 2.0) * static_cast<double>(waves * concurrent) * area;
-            if ((t == 0 && splits == 1) || cost < best_cost * 0.999) {
+            if (!have || cost < best_cost * 0.999) {
                 best = {t, splits};
                 best_cost = cost;
+                have = true;
             }
         }
     }
     return best;
 }
 
-template <int BM, int BN, int RM, int RN, bool VEC_AB>
+template <int BM, int BN, int RM, int RN, bool VEC_AB, bool TF32_ROUND = false>
 cudaError_t launch_ffma_async(const float *a, const float *b, float *c, int m, int k, int n, int splits, bool vec_c,
                               cudaStream_t stream)
 {
@@ -638,10 +649,10 @@ cudaError_t launch_ffma_async(const float *a, const float *b, float *c, int m, i
     const dim3 grid(static_cast<unsigned int>(gx < 65535 ? gx : 65535),
                     static_cast<unsigned int>(gy < 65535 ? gy : 65535), static_cast<unsigned int>(splits));
     if (vec_c)
-        return launch_pdl_cluster_z(ffma_gemm_async_kernel<BM, BN, RM, RN, VEC_AB, true>, grid, dim3(T::kThreads),
-                                    T::kSmemBytes, splits, stream, a, b, c, m, n, k);
-    return launch_pdl_cluster_z(ffma_gemm_async_kernel<BM, BN, RM, RN, VEC_AB, false>, grid, dim3(T::kThreads),
-                                T::kSmemBytes, splits, stream, a, b, c, m, n, k);
+        return launch_pdl_cluster_z(ffma_gemm_async_kernel<BM, BN, RM, RN, VEC_AB, true, TF32_ROUND>, grid,
+                                    dim3(T::kThreads), T::kSmemBytes, splits, stream, a, b, c, m, n, k);
+    return launch_pdl_cluster_z(ffma_gemm_async_kernel<BM, BN, RM, RN, VEC_AB, false, TF32_ROUND>, grid,
+                                dim3(T::kThreads), T::kSmemBytes, splits, stream, a, b, c, m, n, k);
 }
 
 template <bool VEC_AB>
@@ -651,6 +662,30 @@ cudaError_t launch_ffma_plan(const FfmaPlan &plan, const float *a, const float *
     if (plan.tile == 0)
         return launch_ffma_async<128, 128, 8, 8, VEC_AB>(a, b, c, m, k, n, plan.splits, vec_c, stream);
     return launch_ffma_async<32, 32, 4, 4, VEC_AB>(a, b, c, m, k, n, plan.splits, vec_c, stream);
+}
+
+// TF32 problems this small run on the FFMA kernel with each K tile rounded to
+// TF32 in shared memory (the TF32 products are exact in FP32): below about 320^3 the
+// tensor-core path's operand pre-pass and start-up cost more than the FMAs
+// (measured: 64^3-256^3 TF32 at 5.4-7.8 us on the tensor cores, 2.9-4.4 us here).
+bool tf32_on_ffma(int m, int k, int n)
+{
+    return static_cast<int64_t>(m) * k * n <= (int64_t{1} << 25);
+}
+
+// The TF32 form of the FFMA launch: 32 x 32 tiles only.
+int launch_ffma_tf32(const Context *ctx, const float *a, const float *b, float *c, int m, int k, int n,
+                     cudaStream_t stream, char *error, size_t error_size)
+{
+    const bool vec_ab = aligned16(a) && k % 4 == 0 && aligned16(b) && n % 4 == 0;
+    const bool vec_c = aligned16(c) && n % 4 == 0;
+    const FfmaPlan plan = choose_ffma_plan(m, k, n, ctx->sm_count, ctx->ffma_resident, 2u);
+    const cudaError_t st = vec_ab ? launch_ffma_async<32, 32, 4, 4, true, true>(a, b, c, m, k, n, plan.splits, vec_c, stream)
+                                  : launch_ffma_async<32, 32, 4, 4, false, true>(a, b, c, m, k, n, plan.splits, vec_c,
+                                                                                 stream);
+    if (st != cudaSuccess)
+        return fail(error, error_size, "kernel launch", cudaGetErrorString(st));
+    return 0;
 }
 
 int launch_ffma(const Context *ctx, const float *a, const float *b, float *c, int m, int k, int n,
@@ -724,7 +759,8 @@ extern "C" int matmul_kernel_info(int implementation, int precision, char *json,
             "\"b_operand\":\"%s\",\"plan\":\"cost_model\",\"single_cta_kernel\":{\"tile_m\":%d,"
             "\"tile_n\":[256,128,64],\"buffering\":[%d,%d,%d],\"raster_group_m\":%d,"
             "\"split_k\":\"cluster_1x1xS_bulk_copy\",\"max_splits\":8},"
-            "\"skinny_kernel\":{\"when\":\"m<=64\",\"tile_n\":%d,\"max_splits\":8}}",
+            "\"skinny_kernel\":{\"when\":\"m<=64\",\"tile_n\":%d,\"max_splits\":8},"
+            "\"small_tf32\":\"ffma_tf32_rne when m*k*n<=2^25\"}",
             kPrecisionNames[precision], TC2_BM, TC2_BN, TC_ROW_BYTES / elem, TC_THREADS, TC2_HALF, TC2_BN, TC2_HALF,
             TC2_BN, TC2_STAGES, precision == kPrecTf32 ? "tf32" : "f16", TC2_BM, TC2_BN, 32 / elem,
             TC_TMEM_COLUMNS, kRasterGroupMPair, precision == kPrecTf32 ? "rne_prepass" : "none",
@@ -830,6 +866,23 @@ extern "C" void *matmul_create(int device, char *error, size_t error_size)
         B200_FFMA_KERNEL(128, 128, 8, 8, false, true), B200_FFMA_KERNEL(128, 128, 8, 8, false, false),
         B200_FFMA_KERNEL(32, 32, 4, 4, true, true),    B200_FFMA_KERNEL(32, 32, 4, 4, true, false),
         B200_FFMA_KERNEL(32, 32, 4, 4, false, true),   B200_FFMA_KERNEL(32, 32, 4, 4, false, false)};
+    const std::pair<const void *, int> ffma_tf32_kernels[] = {
+        {reinterpret_cast<const void *>(&ffma_gemm_async_kernel<32, 32, 4, 4, true, true, true>),
+         FaTile<32, 32, 4, 4>::kSmemBytes},
+        {reinterpret_cast<const void *>(&ffma_gemm_async_kernel<32, 32, 4, 4, true, false, true>),
+         FaTile<32, 32, 4, 4>::kSmemBytes},
+        {reinterpret_cast<const void *>(&ffma_gemm_async_kernel<32, 32, 4, 4, false, true, true>),
+         FaTile<32, 32, 4, 4>::kSmemBytes},
+        {reinterpret_cast<const void *>(&ffma_gemm_async_kernel<32, 32, 4, 4, false, false, true>),
+         FaTile<32, 32, 4, 4>::kSmemBytes}};
+    for (const auto &kernel : ffma_tf32_kernels) {
+        st = cudaFuncSetAttribute(kernel.first, cudaFuncAttributeMaxDynamicSharedMemorySize, kernel.second);
+        if (st != cudaSuccess) {
+            delete ctx;
+            fail_cuda(error, error_size, "cudaFuncSetAttribute", st);
+            return nullptr;
+        }
+    }
 #undef B200_FFMA_KERNEL
     for (const auto &kernel : ffma_kernels) {
         st = cudaFuncSetAttribute(kernel.first, cudaFuncAttributeMaxDynamicSharedMemorySize, kernel.second);
@@ -1018,6 +1071,12 @@ extern "C" int matmul_plan(void *opaque, int implementation, int precision, int 
                                 static_cast<long long>((n + o.bn - 1) / o.bn),
                                 static_cast<long long>((m + o.bm - 1) / o.bm), plan.splits,
                                 k % 4 == 0 && n % 4 == 0 ? "true" : "false");
+    } else if (precision == kPrecTf32 && tf32_on_ffma(m, k, n)) {
+        const FfmaPlan plan = choose_ffma_plan(m, k, n, ctx->sm_count, ctx->ffma_resident, 2u);
+        written = std::snprintf(json, json_size,
+                                "{\"kernel\":\"ffma_tf32_rne\",\"tile_m\":32,\"tile_n\":32,\"threads\":64,"
+                                "\"splits\":%d,\"cluster\":[1,1,%d]}",
+                                plan.splits, plan.splits);
     } else if (m <= kSkinnyMaxM) {
         const int elem = precision == kPrecTf32 ? 4 : 2;
         const int total_k_blocks = static_cast<int>((static_cast<int64_t>(k) + TC_ROW_BYTES / elem - 1) /

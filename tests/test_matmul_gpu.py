@@ -154,6 +154,10 @@ def test_tcgen05_plans_split_k(native):
     for precision in ("tf32", "fp16", "bf16"):
         for shape in TC_SPLIT_SHAPES:
             plan = native.plan("tcgen05", *shape, precision=precision)
+            m, k, n = shape
+            if precision == "tf32" and m * k * n <= 2 ** 25:
+                assert plan["kernel"] == "ffma_tf32_rne"      # small TF32 problems run on the FFMA pipe
+                continue
             assert plan["kernel"] == "tc_single"
             splits.add(plan["splits"])
     assert splits >= {2, 4, 8}
@@ -283,18 +287,26 @@ def test_graph_of_ten_launches_replays_correctly(native, precision, shape):
     del graph
 
 
-def test_tf32_rounds_halfway_to_even(native):
-    """Bit-exact known answers: reference test_matmul.py:101-111 and test_triton_matmul.py:45-53."""
+@pytest.mark.parametrize("rows", (1, 4096))
+def test_tf32_rounds_halfway_to_even(native, rows):
+    """Bit-exact known answers: reference test_matmul.py:101-111 and test_triton_matmul.py:45-53.
+
+    One row runs on the small-problem FFMA path (K tiles rounded in shared memory),
+    4096 rows x 1024 columns on the tensor cores (operands rounded by the pre-pass)."""
     bits = np.array([0x3f801000, 0x3f803000, 0x3f800fff, 0x3f801001,
                      0xbf801000, 0xbf803000, 0xbf800fff, 0xbf801001], dtype=np.uint32)
-    values = bits.view(np.float32).reshape(1, -1)
+    values = np.tile(bits.view(np.float32).reshape(1, -1), (rows, 1 if rows == 1 else 128))
+    size = values.shape[1]
+    plan = native.plan("tcgen05", rows, size, size, precision="tf32")
+    assert (plan["kernel"] == "ffma_tf32_rne") == (rows == 1)
     a = torch.from_numpy(values).cuda()
-    b = torch.eye(values.size, dtype=torch.float32, device="cuda")
-    out = torch.empty((1, values.size), dtype=torch.float32, device="cuda")
+    b = torch.eye(size, dtype=torch.float32, device="cuda")
+    out = torch.empty((rows, size), dtype=torch.float32, device="cuda")
     native.prepare("tcgen05", a, b, out, precision="tf32")()
-    expected = po.reference_product(values, np.eye(values.size, dtype=np.float32), "tf32")
-    np.testing.assert_array_equal(out.cpu().numpy(), expected)
     np.testing.assert_array_equal(out.cpu().numpy(), po.quantize_inputs(values, "tf32"))
+    if rows == 1:
+        expected = po.reference_product(values, np.eye(size, dtype=np.float32), "tf32")
+        np.testing.assert_array_equal(out.cpu().numpy(), expected)
 
 
 @pytest.mark.parametrize("precision", ("fp16", "bf16"))
