@@ -272,9 +272,10 @@ struct TcPlan {
 // time per K block + epilogue) (+ the split reduction), where a K block costs the
 // most of its MMA time (2 x tile width cycles), its operand bytes at 55 B/cycle
 // into one SM, and all running CTAs' operand bytes at 8 KB/cycle out of L2; a
-// split adds 1000 cycles plus its shared-memory exchange at 8 B/cycle.  Fitted
-// to measured B200 times of every option over square, long-K and skinny shapes
-// in BF16 and TF32 (the chosen plan is within 2.5 % of the fastest on average).
+// split adds 1000 cycles plus its shared-memory exchange at 8 B/cycle, and the
+// CTA pair 6000 cycles of start-up.  Fitted to measured B200 times of every
+// option over square, long-K, skinny and ragged shapes in BF16 and TF32 (the
+// chosen plan is within 3 % of the fastest on average).
 double tc_plan_cycles(const Context *ctx, int m, int k, int n, int prec, int tile_n, int splits)
 {
     constexpr double kStart = 2000.0, kEpilogue = 4000.0, kSmBytes = 55.0, kL2Bytes = 8000.0;
@@ -308,6 +309,8 @@ double tc_plan_cycles(const Context *ctx, int m, int k, int n, int prec, int til
         t_kb = static_cast<double>(active) * bytes_kb / kL2Bytes;
     const double width = tile_n == 0 ? TC2_BN : tile_n;
     double cycles = kStart + static_cast<double>(rounds) * (static_cast<double>(kpb) * t_kb + kEpilogue * width / 256.0);
+    if (tile_n == 0)
+        cycles += 6000.0;       // cluster launch, pair TMEM allocation and teardown
     if (splits > 1)
         cycles += 1000.0 + static_cast<double>(splits - 1) / splits * TC_BM * width * 4.0 / 8.0;
     return cycles;
