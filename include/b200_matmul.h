@@ -119,8 +119,9 @@ int matmul_set_sm_limit(void *context, int sms, char *error, size_t error_size);
  * array compiled into the library (every GPU that loads the library holds it
  * until the process exits).  A problem whose copies need more than 32 MiB is
  * rejected with "matmul_launch_noalloc: this problem needs N bytes of scratch,
- * more than the fixed ..." (TF32 needs 4*(m*k' + n*k') bytes with k' = k
- * rounded up to 4; aligned BF16/FP16 operands need none).  The first call on a
+ * more than the fixed ..." (TF32 above m*k*n = 2^25 needs 4*(m*k' + n*k') bytes
+ * with k' = k rounded up to 4; smaller TF32 problems, split-K launches and
+ * aligned BF16/FP16 operands need none).  The first call on a
  * device looks up the array's device address with that device current; make
  * that first call before any stream capture.  All calls share the one array and
  * every call rewrites the part it uses, so calls that overlap on the GPU (other
