@@ -207,6 +207,7 @@ def single_gpu(args) -> dict:
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
     native = NativeMatmul(device=0)
+    plan = native.plan("tcgen05", 8192, 8192, 8192, precision="bf16")
     stream = torch.cuda.Stream(device=device)
     gen = torch.Generator(device=device)
     gen.manual_seed(2026)
@@ -315,7 +316,7 @@ def single_gpu(args) -> dict:
     traffic = None
     traffic_file = ROOT / "profiles" / "ncu_traffic.json"
     if traffic_file.exists():
-        traffic = json.loads(traffic_file.read_text()).get("tc2_gemm_bf16_8192")
+        traffic = json.loads(traffic_file.read_text()).get(f"{plan['kernel']}_{plan['tile_m']}x{plan['tile_n']}_bf16_8192")
     peak = peaks["bf16_tflops"]
     return {
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
@@ -329,7 +330,7 @@ def single_gpu(args) -> dict:
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "traffic": traffic,
                      "peak_source": f"{peak_kind} bf16_tflops (burst, cuBLAS 8192^3)",
-                     "kernel": "tc2_gemm_kernel<BF16> (CTA pairs)", "kernel_ms": kernel_ms,
+                     "kernel": f"{plan['kernel']} {plan['tile_m']}x{plan['tile_n']} BF16", "kernel_ms": kernel_ms,
                      "algorithmic_flops_per_launch": 2.0 * m * k * n},
         "cpu_baseline": cpu_baseline(),
         "e2e": e2e,

@@ -236,15 +236,19 @@ cudaError_t pack_operands(const Context *ctx, const void *a, bool a_direct, void
                       stream, ja, jb, static_cast<int>(a_blocks));
 }
 
-// tile_n selects the kernel: 0 = CTA pair (256 x 256), else the single-CTA
-// kernel with a 128 x tile_n tile.
+// tile_n selects the kernel: 0 = CTA pair with a 256 x 256 tile, 512 = CTA pair
+// with a 256 x 512 tile, else the single-CTA kernel with a 128 x tile_n tile.
 template <int FMT>
 cudaError_t launch_tc_kernel(int tile_n, int splits, const CUtensorMap &ma, const CUtensorMap &mb,
                              const CUtensorMap &mc, const TcParams &params, int grid, cudaStream_t stream)
 {
     const dim3 block(TC_THREADS);
     if (tile_n == 0)
-        return launch_pdl(tc2_gemm_kernel<FMT>, dim3(grid), block, TC2_SMEM_BYTES, stream, ma, mb, mc, params);
+        return launch_pdl(tc2_gemm_kernel<FMT, TC2_BN>, dim3(grid), block, Tc2Tile<TC2_BN>::kSmem, stream, ma, mb,
+                          mc, params);
+    if (tile_n == TC2W_BN)
+        return launch_pdl(tc2_gemm_kernel<FMT, TC2W_BN>, dim3(grid), block, Tc2Tile<TC2W_BN>::kSmem, stream, ma,
+                          mb, mc, params);
     // Split K: one tile per cluster of `splits` CTAs along z.
     const dim3 g = splits > 1 ? dim3(static_cast<unsigned int>(params.num_tiles), 1, static_cast<unsigned int>(splits))
                               : dim3(static_cast<unsigned int>(grid));
@@ -283,12 +287,14 @@ double tc_plan_cycles(const Context *ctx, int m, int k, int n, int prec, int til
     const int64_t nkb = (static_cast<int64_t>(k) + bk - 1) / bk;
     int64_t tiles, rounds, active;
     double bytes_kb, mma;
-    if (tile_n == 0) {
-        tiles = ((static_cast<int64_t>(m) + TC2_BM - 1) / TC2_BM) * ((static_cast<int64_t>(n) + TC2_BN - 1) / TC2_BN);
+    const bool pair = tile_n == 0 || tile_n == TC2W_BN;
+    const int pair_n = tile_n == TC2W_BN ? TC2W_BN : TC2_BN;
+    if (pair) {
+        tiles = ((static_cast<int64_t>(m) + TC2_BM - 1) / TC2_BM) * ((static_cast<int64_t>(n) + pair_n - 1) / pair_n);
         rounds = (tiles + ctx->max_pairs - 1) / ctx->max_pairs;
         active = 2 * (tiles < ctx->max_pairs ? tiles : ctx->max_pairs);
-        bytes_kb = 2.0 * TC2_HALF * TC_ROW_BYTES;
-        mma = 2.0 * TC2_BN;
+        bytes_kb = static_cast<double>(TC2_HALF + pair_n / 2) * TC_ROW_BYTES;
+        mma = 2.0 * pair_n;
     } else {
         tiles = ((static_cast<int64_t>(m) + TC_BM - 1) / TC_BM) * ((static_cast<int64_t>(n) + tile_n - 1) / tile_n);
         if (splits == 1) {
@@ -307,9 +313,9 @@ double tc_plan_cycles(const Context *ctx, int m, int k, int n, int prec, int til
         t_kb = bytes_kb / kSmBytes;
     if (static_cast<double>(active) * bytes_kb / kL2Bytes > t_kb)
         t_kb = static_cast<double>(active) * bytes_kb / kL2Bytes;
-    const double width = tile_n == 0 ? TC2_BN : tile_n;
+    const double width = pair ? pair_n : tile_n;
     double cycles = kStart + static_cast<double>(rounds) * (static_cast<double>(kpb) * t_kb + kEpilogue * width / 256.0);
-    if (tile_n == 0)
+    if (pair)
         cycles += 10000.0;      // cluster launch, pair TMEM allocation and teardown
     if (splits > 1)
         cycles += 1000.0 + static_cast<double>(splits - 1) / splits * TC_BM * width * 4.0 / 8.0;
@@ -329,8 +335,11 @@ TcPlan choose_tc_plan(const Context *ctx, int m, int k, int n, int prec)
             best_cycles = cycles;
         }
     };
-    if (m > TC_BM && ctx->max_pairs > 0)
+    if (m > TC_BM && ctx->max_pairs > 0) {
         consider(0, 1);
+        if (n > TC2_BN)
+            consider(TC2W_BN, 1);
+    }
     for (int tile_n : {256, 128, 64}) {
         const int64_t tiles =
             ((static_cast<int64_t>(m) + TC_BM - 1) / TC_BM) * ((static_cast<int64_t>(n) + tile_n - 1) / tile_n);
@@ -515,9 +524,9 @@ int launch_tcgen05(Context *ctx, int prec, const void *a, const void *b, float *
 
     const TcPlan plan = choose_tc_plan(ctx, m, k, n, prec);
     const int kernel_n = plan.tile_n;
-    const bool pair = kernel_n == 0;
+    const bool pair = kernel_n == 0 || kernel_n == TC2W_BN;
     const int tile_m = pair ? TC2_BM : TC_BM;
-    const int tile_n = pair ? TC2_BN : kernel_n;
+    const int tile_n = kernel_n == 0 ? TC2_BN : kernel_n;
     const CUtensorMapDataType type = prec == kPrecTf32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                      : prec == kPrecBf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                          : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -762,13 +771,13 @@ extern "C" int matmul_kernel_info(int implementation, int precision, char *json,
             "\"b_operand\":\"%s\",\"plan\":\"cost_model\",\"single_cta_kernel\":{\"tile_m\":%d,"
             "\"tile_n\":[256,128,64],\"buffering\":[%d,%d,%d],\"raster_group_m\":%d,"
             "\"split_k\":\"cluster_1x1xS_bulk_copy\",\"max_splits\":8},"
-            "\"skinny_kernel\":{\"when\":\"m<=64\",\"tile_n\":%d,\"max_splits\":8},"
+            "\"pair_wide_kernel\":{\"tile_n\":%d,\"buffering\":%d,\"accumulator\":\"one, freed in column halves\"},\"skinny_kernel\":{\"when\":\"m<=64\",\"tile_n\":%d,\"max_splits\":8},"
             "\"small_tf32\":\"ffma_tf32_rne when m*k*n<=2^25\"}",
             kPrecisionNames[precision], TC2_BM, TC2_BN, TC_ROW_BYTES / elem, TC_THREADS, TC2_HALF, TC2_BN, TC2_HALF,
             TC2_BN, TC2_STAGES, precision == kPrecTf32 ? "tf32" : "f16", TC2_BM, TC2_BN, 32 / elem,
             TC_TMEM_COLUMNS, kRasterGroupMPair, precision == kPrecTf32 ? "rne_prepass" : "none",
             precision == kPrecTf32 ? "k_major_rounded_transpose" : "mn_major_tma", TC_BM, TcTile<256>::kStages,
-            TcTile<128>::kStages, TcTile<64>::kStages, kRasterGroupM, SK_BM);
+            TcTile<128>::kStages, TcTile<64>::kStages, kRasterGroupM, TC2W_BN, Tc2Tile<TC2W_BN>::kStages, SK_BM);
     } else {
         written = std::snprintf(
             json, json_size,
@@ -924,23 +933,28 @@ extern "C" void *matmul_create(int device, char *error, size_t error_size)
             return nullptr;
         }
     }
-    const void *tc2_kernels[] = {reinterpret_cast<const void *>(&tc2_gemm_kernel<kFmtF16>),
-                                 reinterpret_cast<const void *>(&tc2_gemm_kernel<kFmtBF16>),
-                                 reinterpret_cast<const void *>(&tc2_gemm_kernel<kFmtTF32>)};
-    for (const void *kernel : tc2_kernels) {
-        st = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TC2_SMEM_BYTES);
+    const std::pair<const void *, int> tc2_kernels[] = {
+        {reinterpret_cast<const void *>(&tc2_gemm_kernel<kFmtF16, TC2_BN>), Tc2Tile<TC2_BN>::kSmem},
+        {reinterpret_cast<const void *>(&tc2_gemm_kernel<kFmtBF16, TC2_BN>), Tc2Tile<TC2_BN>::kSmem},
+        {reinterpret_cast<const void *>(&tc2_gemm_kernel<kFmtTF32, TC2_BN>), Tc2Tile<TC2_BN>::kSmem},
+        {reinterpret_cast<const void *>(&tc2_gemm_kernel<kFmtF16, TC2W_BN>), Tc2Tile<TC2W_BN>::kSmem},
+        {reinterpret_cast<const void *>(&tc2_gemm_kernel<kFmtBF16, TC2W_BN>), Tc2Tile<TC2W_BN>::kSmem},
+        {reinterpret_cast<const void *>(&tc2_gemm_kernel<kFmtTF32, TC2W_BN>), Tc2Tile<TC2W_BN>::kSmem}};
+    for (const auto &kernel : tc2_kernels) {
+        st = cudaFuncSetAttribute(kernel.first, cudaFuncAttributeMaxDynamicSharedMemorySize, kernel.second);
         if (st != cudaSuccess) {
             delete ctx;
             fail_cuda(error, error_size, "cudaFuncSetAttribute", st);
             return nullptr;
         }
     }
-    // How many 2-CTA clusters of the pair kernel fit on the device at once.
-    {
+    // How many 2-CTA clusters of the pair kernels (both widths) fit on the device at once.
+    ctx->max_pairs = -1;
+    for (int i : {1, 4}) {
         cudaLaunchConfig_t config{};
         config.gridDim = dim3(2 * (sms / 2), 1, 1);
         config.blockDim = dim3(TC_THREADS, 1, 1);
-        config.dynamicSmemBytes = TC2_SMEM_BYTES;
+        config.dynamicSmemBytes = static_cast<size_t>(tc2_kernels[i].second);
         cudaLaunchAttribute attribute{};
         attribute.id = cudaLaunchAttributeClusterDimension;
         attribute.val.clusterDim.x = 2;
@@ -949,12 +963,13 @@ extern "C" void *matmul_create(int device, char *error, size_t error_size)
         config.attrs = &attribute;
         config.numAttrs = 1;
         int clusters = 0;
-        st = cudaOccupancyMaxActiveClusters(&clusters, tc2_kernels[1], &config);
+        st = cudaOccupancyMaxActiveClusters(&clusters, tc2_kernels[i].first, &config);
         if (st != cudaSuccess) {
             cudaGetLastError();
             clusters = 0;
         }
-        ctx->max_pairs = clusters;
+        if (ctx->max_pairs < 0 || clusters < ctx->max_pairs)
+            ctx->max_pairs = clusters;
     }
     // ... and how many CTAs of the single-CTA kernel in split-K clusters of 2, 4, 8.
     ctx->max_split_ctas[0] = ctx->sm_count;
@@ -1089,19 +1104,19 @@ extern "C" int matmul_plan(void *opaque, int implementation, int precision, int 
                                 m <= 16 ? 16 : m <= 32 ? 32 : 64, SK_BM, skinny_splits(ctx, n, total_k_blocks));
     } else {
         const TcPlan plan = choose_tc_plan(ctx, m, k, n, precision);
-        const int64_t tiles =
-            plan.tile_n == 0
-                ? ((static_cast<int64_t>(m) + TC2_BM - 1) / TC2_BM) * ((static_cast<int64_t>(n) + TC2_BN - 1) / TC2_BN)
-                : ((static_cast<int64_t>(m) + TC_BM - 1) / TC_BM) *
-                      ((static_cast<int64_t>(n) + plan.tile_n - 1) / plan.tile_n);
-        const int64_t ctas = plan.tile_n == 0 ? 2 * (tiles < ctx->max_pairs ? tiles : ctx->max_pairs)
+        const bool pair = plan.tile_n == 0 || plan.tile_n == TC2W_BN;
+        const int tile_m = pair ? TC2_BM : TC_BM;
+        const int tile_n = plan.tile_n == 0 ? TC2_BN : plan.tile_n;
+        const int64_t tiles = ((static_cast<int64_t>(m) + tile_m - 1) / tile_m) *
+                              ((static_cast<int64_t>(n) + tile_n - 1) / tile_n);
+        const int64_t ctas = pair ? 2 * (tiles < ctx->max_pairs ? tiles : ctx->max_pairs)
                              : plan.splits > 1 ? tiles * plan.splits
                                                : (tiles < ctx->sm_count ? tiles : ctx->sm_count);
-        written = plan.tile_n == 0
+        written = pair
                       ? std::snprintf(json, json_size,
                                       "{\"kernel\":\"tc2_pair\",\"tile_m\":%d,\"tile_n\":%d,\"cluster\":[2,1,1],"
                                       "\"splits\":1,\"ctas\":%lld}",
-                                      TC2_BM, TC2_BN, static_cast<long long>(ctas))
+                                      TC2_BM, tile_n, static_cast<long long>(ctas))
                       : std::snprintf(json, json_size,
                                       "{\"kernel\":\"tc_single\",\"tile_m\":%d,\"tile_n\":%d,\"splits\":%d,"
                                       "\"cluster\":[1,1,%d],\"ctas\":%lld}",

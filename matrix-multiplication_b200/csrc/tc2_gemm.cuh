@@ -1,15 +1,28 @@
 // CTA-pair (cta_group::2) variant of the tcgen05 GEMM: one 2-CTA cluster computes
-// a 256 x 256 output tile with tcgen05.mma.cta_group::2 (M = 256, N = 256).
+// a 256 x BN output tile (BN = 256 or 512) with tcgen05.mma.cta_group::2
+// instructions of M = 256, N = 256 (BN / 256 of them per K step).
 //
 // Split of the tile across the pair (rank r = %cluster_ctarank, 0 = leader):
 //   * A: CTA r stages rows [m0 + 128 r, m0 + 128 r + 128) of the K slice;
-//   * B: CTA r stages columns [n0 + 128 r, n0 + 128 r + 128);
-//   * D: CTA r's TMEM holds output rows m0 + 128 r .. +127, all 256 columns.
+//   * B: for each 256-column half h of the tile, CTA r stages columns
+//     [n0 + 256 h + 128 r, +128);
+//   * D: CTA r's TMEM holds output rows m0 + 128 r .. +127, all BN columns
+//     (TMEM column c = output column n0 + c).
 // Both CTAs keep their operands at the same shared-memory offsets; the leader's
 // descriptors name its own copy and the tensor cores of the pair read both.
-// Each SM therefore stages and reads 32 KB per 256 x 256 x 64 step instead of
-// 48 KB per 128 x 256 x 64 in the single-CTA kernel, which is what lets the
-// pair run closer to the tensor-core rate.
+//
+// Operand bytes an SM stages per K block against its MMA cycles decide the rate:
+// BN = 256 stages 32 KB per 512 cycles (64 B/cycle, more than the ~55 B/cycle an
+// SM takes in from L2, so the tensor pipe idles ~10 %), BN = 512 stages 48 KB per
+// 1024 cycles (48 B/cycle).  BN = 256 double-buffers its accumulator in TMEM (2 x
+// 256 columns); BN = 512 fills all 512 columns with one accumulator, so the
+// accumulator is handed over in two column halves.  In the last kDefer K blocks
+// of a tile the MMA thread issues the column 0-255 MMAs first and commits that
+// half, so the epilogue reads it while the column 256-511 MMAs of those blocks
+// run; the next tile starts on columns 0-255 and holds back its column 256-511
+// MMAs of the first kDefer K blocks (their stages stay resident) until the
+// epilogue has read those columns too.  The K order of every sum is unchanged,
+// so both widths give the same bits (1-3 deferred blocks measured alike).
 //
 // Synchronisation (all waits bounded, see ptx.cuh):
 //   full[s]   leader only; the leader's producer arms it with both CTAs' bytes,
@@ -17,8 +30,10 @@
 //   empty[s]  in both CTAs; one multicast tcgen05.commit from the leader's MMA
 //             thread arrives on both (two separate commits per stage cost ~10 %
 //             of tensor-pipe time in the issue loop).
-//   accf[i]   in both CTAs; committed the same way when accumulator i is done.
-//   acce[i]   leader only; one arrive per epilogue warp of both CTAs (8).
+//   accf[i]   in both CTAs; committed the same way when accumulator i is done
+//             (BN = 512: accf[0] only).
+//   acce[i]   leader only; one arrive per epilogue warp of both CTAs (8) when
+//             accumulator i (BN = 512: column half i) has been read.
 // Warp roles and the epilogue are those of the single-CTA kernel (tc_gemm.cuh).
 // No load uses cluster multicast: every CTA fetches its own tiles.
 #pragma once
@@ -32,19 +47,36 @@
 namespace b200 {
 
 constexpr int TC2_BM = 256;                 // rows per pair tile
-constexpr int TC2_BN = 256;                 // columns per pair tile
-constexpr int TC2_HALF = 128;               // rows (A) / columns (B) staged per CTA
-constexpr int TC2_STAGES = 6;
+constexpr int TC2_BN = 256;                 // columns per pair tile (narrow kernel)
+constexpr int TC2W_BN = 512;                // columns per pair tile (wide kernel)
+constexpr int TC2_HALF = 128;               // rows (A) / columns of a B half staged per CTA
 constexpr int TC2_A_STAGE = TC2_HALF * TC_ROW_BYTES;   // 16 KB
-constexpr int TC2_B_STAGE = TC2_HALF * TC_ROW_BYTES;   // 16 KB
-constexpr int TC2_SMEM_BYTES =
-    1024 + TC2_STAGES * (TC2_A_STAGE + TC2_B_STAGE) + TC_EPI_BYTES + TC_BAR_BYTES;
 
-template <int FMT>
+template <int BN>
+struct Tc2Tile {
+    static_assert(BN == 256 || BN == 512, "pair tile width");
+    static constexpr int kHalves = BN / 256;                        // N = 256 MMAs per K step
+    static constexpr int kBStage = kHalves * TC2_HALF * TC_ROW_BYTES;   // 16 or 32 KB
+    static constexpr int kStages = BN == 256 ? 6 : 4;
+    static constexpr int kAccs = BN == 256 ? 2 : 1;                 // TMEM accumulators of BN columns
+    static constexpr int kSmem = 1024 + kStages * (TC2_A_STAGE + kBStage) + TC_EPI_BYTES + TC_BAR_BYTES;
+};
+constexpr int TC2_STAGES = Tc2Tile<TC2_BN>::kStages;
+constexpr int TC2_SMEM_BYTES = Tc2Tile<TC2_BN>::kSmem;
+static_assert(Tc2Tile<TC2W_BN>::kSmem <= 227 * 1024, "wide pair tile exceeds shared memory");
+
+template <int FMT, int BN = TC2_BN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
 tc2_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                 const __grid_constant__ CUtensorMap map_c, const TcParams p)
 {
+    using Tile = Tc2Tile<BN>;
+    constexpr int kStages = Tile::kStages;
+    constexpr int kHalves = Tile::kHalves;
+    constexpr int kBStage = Tile::kBStage;
+    constexpr int kAccs = Tile::kAccs;
+    constexpr int kDefer = 2;     // BN = 512: K blocks at each end of a tile run on one column half first
+    static_assert(kDefer >= 1 && kDefer < kStages, "deferred K blocks must leave the producer a stage");
     constexpr bool kTF32 = FMT == kFmtTF32;
     constexpr int kElem = kTF32 ? 4 : 2;
     constexpr int kBK = TC_ROW_BYTES / kElem;          // K elements per stage (64 or 32)
@@ -54,22 +86,23 @@ tc2_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
     constexpr int kBBoxes = TC2_HALF / kNB;            // 2 boxes per CTA half (MN-major B)
     constexpr uint32_t kBBoxBytes = kBK * TC_ROW_BYTES;
     constexpr bool kBKMajor = kTF32;
-    constexpr uint32_t kIdesc = tc_instr_desc(FMT, kBKMajor, TC2_BM, TC2_BN);
-    constexpr uint32_t kStageTx = 2u * (TC2_A_STAGE + TC2_B_STAGE);   // both CTAs
+    constexpr uint32_t kIdesc = tc_instr_desc(FMT, kBKMajor, TC2_BM, 256);
+    constexpr uint32_t kBHalfBytes = TC2_HALF * TC_ROW_BYTES;         // one 128-column B half of a CTA
+    constexpr uint32_t kStageTx = 2u * (TC2_A_STAGE + kBStage);       // both CTAs
 
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_addr(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
     const uint32_t s_a = base;
-    const uint32_t s_b = s_a + TC2_STAGES * TC2_A_STAGE;
-    const uint32_t s_epi = s_b + TC2_STAGES * TC2_B_STAGE;
+    const uint32_t s_b = s_a + kStages * TC2_A_STAGE;
+    const uint32_t s_epi = s_b + kStages * kBStage;
     const uint32_t s_bar = s_epi + TC_EPI_BYTES;
     auto full_bar = [&](int s) { return s_bar + 8u * s; };
-    auto empty_bar = [&](int s) { return s_bar + 8u * (TC2_STAGES + s); };
-    auto accf_bar = [&](int i) { return s_bar + 8u * (2 * TC2_STAGES + i); };
-    auto acce_bar = [&](int i) { return s_bar + 8u * (2 * TC2_STAGES + 2 + i); };
-    const uint32_t drain_bar = s_bar + 8u * (2 * TC2_STAGES + 4);
-    const uint32_t tmem_slot = s_bar + 8u * (2 * TC2_STAGES + 5);
+    auto empty_bar = [&](int s) { return s_bar + 8u * (kStages + s); };
+    auto accf_bar = [&](int i) { return s_bar + 8u * (2 * kStages + i); };
+    auto acce_bar = [&](int i) { return s_bar + 8u * (2 * kStages + 2 + i); };
+    const uint32_t drain_bar = s_bar + 8u * (2 * kStages + 4);
+    const uint32_t tmem_slot = s_bar + 8u * (2 * kStages + 5);
     uint32_t *tmem_slot_ptr = reinterpret_cast<uint32_t *>(smem_raw + (tmem_slot - raw));
 
     const int warp = threadIdx.x >> 5;
@@ -80,7 +113,7 @@ tc2_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
     const int pairs = gridDim.x >> 1;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < TC2_STAGES; ++s) {
+        for (int s = 0; s < kStages; ++s) {
             mbar_init(full_bar(s), 1);
             mbar_init(empty_bar(s), 1);
         }
@@ -121,7 +154,7 @@ tc2_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
                 int mb, nb;
                 tc_tile_coords(tile, p, mb, nb);
                 const int a_row = mb * TC2_BM + static_cast<int>(rank) * TC2_HALF;
-                const int b_col = nb * TC2_BN + static_cast<int>(rank) * TC2_HALF;
+                const int b_col = nb * BN + static_cast<int>(rank) * TC2_HALF;
                 for (int kb = 0; kb < p.num_k_blocks; ++kb) {
                     if (!mbar_wait(empty_bar(stage), phase ^ 1u)) {
                         report_status(kStatusLoadTimeout);
@@ -132,24 +165,28 @@ tc2_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
                     if (leader)
                         mbar_arrive_expect_tx(full_bar(stage), kStageTx);
                     tma_load_2d_pair(s_a + stage * TC2_A_STAGE, &map_a, fb, kb * kBK, a_row);
-                    if constexpr (kBKMajor) {
-                        tma_load_2d_pair(s_b + stage * TC2_B_STAGE, &map_b, fb, kb * kBK, b_col);
-                    } else {
 #pragma unroll
-                        for (int j = 0; j < kBBoxes; ++j)
-                            tma_load_2d_pair(s_b + stage * TC2_B_STAGE + j * kBBoxBytes, &map_b, fb, b_col + j * kNB,
-                                             kb * kBK);
+                    for (int h = 0; h < kHalves; ++h) {
+                        const uint32_t s_bh = s_b + stage * kBStage + h * kBHalfBytes;
+                        if constexpr (kBKMajor) {
+                            tma_load_2d_pair(s_bh, &map_b, fb, kb * kBK, b_col + h * 256);
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < kBBoxes; ++j)
+                                tma_load_2d_pair(s_bh + j * kBBoxBytes, &map_b, fb, b_col + h * 256 + j * kNB,
+                                                 kb * kBK);
+                        }
                     }
                     filled |= 1u << stage;
                     fill_parity = (fill_parity & ~(1u << stage)) | (phase << stage);
-                    if (++stage == TC2_STAGES) {
+                    if (++stage == kStages) {
                         stage = 0;
                         phase ^= 1u;
                     }
                 }
             }
             if (leader) {
-                for (int s = 0; s < TC2_STAGES; ++s)
+                for (int s = 0; s < kStages; ++s)
                     if ((filled >> s) & 1u)
                         if (!mbar_wait(full_bar(s), (fill_parity >> s) & 1u))
                             report_status(kStatusDrainTimeout);
@@ -166,9 +203,19 @@ tc2_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
             const uint64_t a_desc0 = smem_desc_sw128(s_a, 16, 1024);
             const uint64_t b_desc0 = kBKMajor ? smem_desc_sw128(s_b, 16, 1024) : smem_desc_sw128(s_b, kBBoxBytes, 1024);
             constexpr uint64_t kADescStage = TC2_A_STAGE >> 4;
-            constexpr uint64_t kBDescStage = TC2_B_STAGE >> 4;
+            constexpr uint64_t kBDescStage = kBStage >> 4;
+            constexpr uint64_t kBDescHalf = kBHalfBytes >> 4;
             constexpr uint64_t kADescK = 32 >> 4;
             constexpr uint64_t kBDescK = kBKMajor ? (32 >> 4) : ((kMmaK * TC_ROW_BYTES) >> 4);
+            // The MMAs of one K block for one 256-column half of the accumulator.
+            auto issue_half = [&](uint32_t d_tmem, int s, int h, int kb) {
+                const uint64_t a_desc = a_desc0 + static_cast<uint64_t>(s) * kADescStage;
+                const uint64_t b_desc = b_desc0 + static_cast<uint64_t>(s) * kBDescStage + h * kBDescHalf;
+#pragma unroll
+                for (int kk = 0; kk < kMmasPerStage; ++kk)
+                    tc_mma_pair<kTF32>(d_tmem + static_cast<uint32_t>(h * 256), a_desc + kk * kADescK,
+                                       b_desc + kk * kBDescK, kIdesc, (kb | kk) != 0 ? 1u : 0u);
+            };
             int acc = 0;
             uint32_t acc_phase = 0;
             bool ok = true;
@@ -178,31 +225,64 @@ tc2_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
                     break;
                 }
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * TC2_BN);
-                for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+                const int nkb = p.num_k_blocks;
+                bool upper_live = false;              // BN = 512: the epilogue has read columns 256-511
+                int pending = 0, pending_stage = 0;   // BN = 512: K blocks whose column 256-511 MMAs wait
+                for (int kb = 0; kb < nkb; ++kb) {
                     if (!mbar_wait(full_bar(stage), phase)) {
                         report_status(kStatusMmaTimeout);
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t a_desc = a_desc0 + static_cast<uint64_t>(stage) * kADescStage;
-                    const uint64_t b_desc = b_desc0 + static_cast<uint64_t>(stage) * kBDescStage;
-#pragma unroll
-                    for (int kk = 0; kk < kMmasPerStage; ++kk)
-                        tc_mma_pair<kTF32>(d_tmem, a_desc + kk * kADescK, b_desc + kk * kBDescK, kIdesc,
-                                      (kb | kk) != 0 ? 1u : 0u);
-                    // Free this stage in both CTAs (one multicast commit).
-                    tc_commit_pair_both(empty_bar(stage), 3);
-                    if (++stage == TC2_STAGES) {
+                    issue_half(d_tmem, stage, 0, kb);
+                    if constexpr (kHalves == 1) {
+                        // Free this stage in both CTAs (one multicast commit).
+                        tc_commit_pair_both(empty_bar(stage), 3);
+                    } else {
+                        if (kb == nkb - 1)
+                            tc_commit_pair_both(accf_bar(0), 3);    // columns 0-255 complete
+                        if (upper_live && kb < nkb - kDefer) {
+                            issue_half(d_tmem, stage, 1, kb);
+                            tc_commit_pair_both(empty_bar(stage), 3);
+                        } else {
+                            // The first kDefer K blocks (columns 256-511 still being read)
+                            // and the last kDefer (columns 0-255 finish first, so their
+                            // epilogue overlaps these MMAs) wait; then catch up, oldest
+                            // first, and free their stages.
+                            if (pending++ == 0)
+                                pending_stage = stage;
+                            if (kb == nkb - 1 || (!upper_live && kb == kDefer - 1)) {
+                                if (!upper_live) {
+                                    if (!mbar_wait(acce_bar(1), acc_phase ^ 1u)) {
+                                        report_status(kStatusMmaTimeout);
+                                        ok = false;
+                                        break;
+                                    }
+                                    tc_fence_after();
+                                    upper_live = true;
+                                }
+                                int s = pending_stage;
+                                for (int j = kb - pending + 1; j <= kb; ++j) {
+                                    issue_half(d_tmem, s, 1, j);
+                                    tc_commit_pair_both(empty_bar(s), 3);
+                                    if (++s == kStages)
+                                        s = 0;
+                                }
+                                pending = 0;
+                            }
+                        }
+                    }
+                    if (++stage == kStages) {
                         stage = 0;
                         phase ^= 1u;
                     }
                 }
                 if (!ok)
                     break;
-                tc_commit_pair_both(accf_bar(acc), 3);
-                if (++acc == 2) {
+                tc_commit_pair_both(accf_bar(kHalves == 1 ? acc : 1), 3);
+                if (++acc == kAccs) {
                     acc = 0;
                     acc_phase ^= 1u;
                 }
@@ -218,33 +298,40 @@ tc2_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
         int acc = 0;
         uint32_t acc_phase = 0;
         uint32_t stores = 0;
-        for (int tile = pair; tile < p.num_tiles; tile += pairs) {
-            int mb, nb;
-            tc_tile_coords(tile, p, mb, nb);
+        // All four epilogue warps wait for accumulator (half) i to be complete.
+        auto wait_accf = [&](int i) {
             int ok = 1;
             if (lane == 0)
-                ok = mbar_wait(accf_bar(acc), acc_phase) ? 1 : 0;
+                ok = mbar_wait(accf_bar(i), acc_phase) ? 1 : 0;
             ok = epilogue_all(__shfl_sync(0xffffffffu, ok, 0));
-            if (!ok) {
-                if (lane == 0)
-                    report_status(kStatusEpilogueTimeout);
-                break;
-            }
+            if (!ok && lane == 0)
+                report_status(kStatusEpilogueTimeout);
             tc_fence_after();
+            return ok != 0;
+        };
+        bool ok = true;
+        for (int tile = pair; ok && tile < p.num_tiles; tile += pairs) {
+            int mb, nb;
+            tc_tile_coords(tile, p, mb, nb);
+            if (!wait_accf(kAccs == 2 ? acc : 0))
+                break;
             const int tile_row0 = mb * TC2_BM + static_cast<int>(rank) * TC2_HALF;   // first row of this CTA's part of the tile
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
-                                   static_cast<uint32_t>(acc * TC2_BN);
+                                   static_cast<uint32_t>(acc * BN);
 #pragma unroll 1
-            for (int chunk = 0; chunk < TC2_BN / 32; ++chunk) {
+            for (int chunk = 0; chunk < BN / 32; ++chunk) {
+                if (kAccs == 1 && chunk == 8 && !(ok = wait_accf(1)))     // BN = 512: columns 256-511
+                    break;
                 uint32_t v[32];
                 tmem_load_32cols(t_row + chunk * 32, v);
-                if (chunk == TC2_BN / 32 - 1) {
+                if (chunk % 8 == 7) {
+                    // Accumulator `acc` (BN = 256) or column half chunk / 8 (BN = 512) read.
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0)
-                        mbar_arrive_cluster(map_to_cta(acce_bar(acc), 0));
+                        mbar_arrive_cluster(map_to_cta(acce_bar(kAccs == 2 ? acc : chunk / 8), 0));
                 }
-                const int col0 = nb * TC2_BN + chunk * 32;
+                const int col0 = nb * BN + chunk * 32;
                 if (col0 >= p.n || tile_row0 >= p.m)      // the same for all four warps
                     continue;
                 if (!p.c_direct) {
@@ -291,7 +378,7 @@ tc2_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
                     ++stores;
                 }
             }
-            if (++acc == 2) {
+            if (++acc == kAccs) {
                 acc = 0;
                 acc_phase ^= 1u;
             }

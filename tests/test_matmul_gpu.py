@@ -164,6 +164,29 @@ def test_tcgen05_plans_split_k(native):
     assert native.plan("tcgen05", 8192, 8192, 8192, precision="bf16")["kernel"] == "tc2_pair"
 
 
+# Shapes the launch plan gives the 256 x 512 CTA-pair tile (one accumulator freed
+# in column halves, deferred upper-half MMAs at both ends of every tile).
+WIDE_PAIR_SHAPES = ((3001, 2048, 5003), (2048, 1024, 4096), (1537, 777, 3001))
+
+
+def test_wide_pair_plans(native):
+    for m, k, n in WIDE_PAIR_SHAPES + ((8192, 8192, 8192), (4096, 14336, 4096)):
+        for precision in ("tf32", "fp16", "bf16"):
+            if (m, k, n) == (1537, 777, 3001) and precision != "tf32":
+                continue
+            plan = native.plan("tcgen05", m, k, n, precision=precision)
+            assert (plan["kernel"], plan["tile_m"], plan["tile_n"]) == ("tc2_pair", 256, 512), (m, k, n, plan)
+
+
+@pytest.mark.parametrize("precision", ("tf32", "fp16", "bf16"))
+@pytest.mark.parametrize("shape", WIDE_PAIR_SHAPES)
+def test_wide_pair_against_fp64_oracle(native, precision, shape):
+    m, k, n = shape
+    a_np = po.seeded_uniform((m, k), seed=17 * m + k)
+    b_np = po.seeded_uniform((k, n), seed=19 * n + k)
+    _run_and_verify(native, "tcgen05", precision, a_np, b_np, offset=shape[1] % 2 == 1, runs=1)
+
+
 @pytest.mark.parametrize("precision", ("tf32", "fp16", "bf16"))
 @pytest.mark.parametrize("shape", TC_SPLIT_SHAPES)
 def test_tcgen05_split_k_against_fp64_oracle(native, precision, shape):
