@@ -93,10 +93,12 @@ int matmul_check_fp64(void *context, int precision, const void *a, const void *b
 /* No counterpart in the reference (the nearest is matmul_kernel_info, which
  * describes a kernel, not a launch).  Writes, as a JSON object, the launch that
  * matmul_launch would make for an m x k x n problem on this context's device:
- * "kernel" (tc2_pair, tc_single, tc_skinny, ffma_async or ffma_generic),
- * "tile_m", "tile_n", "splits" (K slices summed in a fixed order) and, where
- * they apply, "cluster", "threads" and "grid".  The FFMA plan assumes 16-byte
- * aligned base pointers.  Needs no stream and launches nothing. */
+ * "kernel" (tc2_pair with a 256 x 256 or 256 x 512 tile, tc_single,
+ * tc_skinny, ffma_async, or ffma_tf32_rne for small TF32 problems), "tile_m",
+ * "tile_n", "splits" (K slices summed in a fixed order) and, where they apply,
+ * "cluster", "threads", "grid" and "vector_loads_if_aligned" (FFMA: 16-byte
+ * copies when the base pointers are 16-byte aligned too).  Needs no stream and
+ * launches nothing. */
 int matmul_plan(void *context, int implementation, int precision, int m, int k, int n, char *json,
                 size_t json_size, char *error, size_t error_size);
 

@@ -267,7 +267,7 @@ cudaError_t launch_tc_kernel(int tile_n, int splits, const CUtensorMap &ma, cons
 }
 
 struct TcPlan {
-    int tile_n;   // 0 = CTA pair (256 x 256), else the single-CTA tile width
+    int tile_n;   // 0 = CTA pair (256 x 256), TC2W_BN = CTA pair (256 x 512), else the single-CTA tile width
     int splits;   // K splits (clusters of splits CTAs along z); single-CTA kernel only
 };
 
