@@ -196,15 +196,20 @@ def test_tcgen05_split_k_against_fp64_oracle(native, precision, shape):
     _run_and_verify(native, "tcgen05", precision, a_np, b_np, offset=False)
 
 
-def test_sm_limit_bounds_the_launch_and_keeps_results(native):
-    m, k, n = 2048, 1024, 3072
+@pytest.mark.parametrize("shape,sms", (((2048, 1024, 3072), 40), ((4096, 2048, 4096), 132)))
+def test_sm_limit_bounds_the_launch_and_keeps_results(native, shape, sms):
+    """132 SMs is what the row-sharded multi-GPU step leaves the GEMM (16 reserved for
+    NCCL); that shape runs on the 256 x 512 pair tile."""
+    m, k, n = shape
     full = native.plan("tcgen05", m, k, n, precision="bf16")
     a_np = po.seeded_uniform((m, k), 21)
     b_np = po.seeded_uniform((k, n), 22)
     try:
-        native.set_sm_limit(40)
+        native.set_sm_limit(sms)
         limited = native.plan("tcgen05", m, k, n, precision="bf16")
-        assert limited["ctas"] <= 40 < full["ctas"]
+        assert limited["ctas"] <= sms < full["ctas"]
+        if sms == 132:
+            assert (limited["kernel"], limited["tile_n"]) == ("tc2_pair", 512)
         _run_and_verify(native, "tcgen05", "bf16", a_np, b_np, offset=False, runs=1)
         with pytest.raises(RuntimeError):
             native.set_sm_limit(1)
