@@ -596,8 +596,9 @@ def test_reference_library_agrees(native):
     lib.matmul_destroy(ctx, err, len(err))
 
 
-@pytest.mark.parametrize("precision,chunks", [("bf16", 4), ("tf32", 3), ("fp32", 2), ("fp16", 1)])
-def test_host_to_host_pipeline(native, precision, chunks):
+@pytest.mark.parametrize("precision,chunks,tail", [("bf16", 4, 1), ("bf16", 3, 4), ("tf32", 3, 2), ("fp32", 2, 1),
+                                                   ("fp16", 1, 1)])
+def test_host_to_host_pipeline(native, precision, chunks, tail):
     """end_to_end.HostMatmul: FP32 host inputs, on-device conversion, chunked GEMM
     and overlapped copies give the oracle's answer in a pinned host buffer."""
     from end_to_end import HostMatmul
@@ -605,7 +606,9 @@ def test_host_to_host_pipeline(native, precision, chunks):
     m, k, n = 1000, 384, 520
     a_np = po.seeded_uniform((m, k), 41)
     b_np = po.seeded_uniform((k, n), 42)
-    host_gemm = HostMatmul(native, m, k, n, precision, chunks=chunks)
+    host_gemm = HostMatmul(native, m, k, n, precision, chunks=chunks, tail_chunks=tail)
+    assert [r for r in host_gemm.ranges if r[1] <= r[0]] == [] and host_gemm.ranges[-1][1] == m
+    assert len(host_gemm.ranges) == chunks - 1 + tail
     a = torch.from_numpy(a_np).pin_memory()
     b = torch.from_numpy(b_np).pin_memory()
     c = torch.full((m, n), float("nan"), dtype=torch.float32).pin_memory()
