@@ -187,14 +187,6 @@ def cpu_baseline(seconds: float = 10.0) -> dict:
 
 
 # ---------------------------------------------------------------- single GPU
-def reference_method(run, stream, m, k, n, warmup=10, repeats=21) -> dict:
-    from benchmark_backends import measure_cuda_device
-
-    samples = measure_cuda_device(run, stream, warmup, repeats)
-    median = statistics.median(samples)
-    return {"median_ms": median, "tflops": tflops(m, k, n, median)}
-
-
 def capture_graph_timer(call, stream, warmup=10):
     """One graph of DEVICE_BATCH calls between external events, after `warmup`
     eager calls: the capture half of the reference's measure_cuda_device
@@ -340,14 +332,18 @@ def single_gpu(args) -> dict:
                     native.convert(a32, pa, precision)
                     native.convert(b32, pb, precision)
                 prun = native.prepare(backend, pa, pb, c, precision=precision)
-            per_precision[precision] = dict(backend=backend, **reference_method(prun, stream, m, k, n))
+            ours_timer = capture_graph_timer(prun, stream)
             with torch_precision(torch, precision):
                 if precision in ("fp16", "bf16"):
                     trun = lambda pa=pa, pb=pb: torch.mm(pa, pb, out_dtype=torch.float32, out=c)
                 else:
                     trun = lambda pa=pa, pb=pb: torch.mm(pa, pb, out=c)
-                cublas[precision] = reference_method(trun, stream, m, k, n)
-            del pa, pb, prun
+                theirs_timer = capture_graph_timer(trun, stream)
+            # The reference's statistic for both arms, their graph replays alternating.
+            ours, theirs = interleaved_reference_method([ours_timer, theirs_timer], m, k, n)
+            per_precision[precision] = dict(backend=backend, **ours)
+            cublas[precision] = theirs
+            del pa, pb, prun, ours_timer, theirs_timer
         ffma_peak = SM_COUNT * FFMA_PER_SM_PER_CLK * 2 * peaks.get("sm_max_mhz", 1965.0) * 1e6 / 1e12
         per_precision["fp32"]["ffma_peak_tflops_at_max_clock"] = ffma_peak
         per_precision["fp32"]["frac_of_ffma_peak"] = per_precision["fp32"]["tflops"] / ffma_peak
