@@ -1,4 +1,4 @@
-"""The reference's CPU GEMM backends, restated (TEST / BASELINE INFRASTRUCTURE ONLY).
+"""The reference's CPU GEMM backends, restated (TEST AND CPU-BASELINE INFRASTRUCTURE ONLY).
 
 Only ``bench.py``'s CPU-baseline leg and ``--impl reference`` arm call this;
 the product never does.  It restates the two CPU backends of
