@@ -29,6 +29,16 @@ from precision import BACKEND_PRECISIONS, INPUT_DTYPES
 from sharded import chunk_rows
 
 
+def row_blocks(m: int, chunks: int, tail_chunks: int = 1) -> list[tuple[int, int]]:
+    """Contiguous, non-empty row blocks covering [0, m): ``chunks`` near-equal blocks
+    with the last one split again into up to ``tail_chunks``."""
+    ranges = chunk_rows(m, chunks)
+    if tail_chunks > 1 and ranges:
+        lo, hi = ranges.pop()
+        ranges += [(lo + a, lo + b) for a, b in chunk_rows(hi - lo, tail_chunks)]
+    return ranges
+
+
 class HostMatmul:
     """C (host, FP32) = A (host, FP32) * B (host, FP32) computed in ``precision`` on one GPU."""
 
@@ -42,11 +52,7 @@ class HostMatmul:
             raise ValueError(f"{self.backend} does not support {precision}")
         self.device = torch.device("cuda", native.device)
         dtype = getattr(torch, INPUT_DTYPES[precision])
-        ranges = chunk_rows(m, chunks)
-        if tail_chunks > 1 and ranges:
-            lo, hi = ranges.pop()
-            ranges += [(lo + a, lo + b) for a, b in chunk_rows(hi - lo, tail_chunks)]
-        self.ranges = ranges
+        self.ranges = row_blocks(m, chunks, tail_chunks)
         self.a32 = torch.empty((m, k), dtype=torch.float32, device=self.device)
         self.b32 = torch.empty((k, n), dtype=torch.float32, device=self.device)
         if precision == "fp32":

@@ -35,6 +35,25 @@ def test_chunk_rows():
     assert chunk_rows(0, 4) == []
 
 
+@pytest.mark.parametrize("m,chunks,tail", [(8192, 8, 2), (8192, 8, 4), (1000, 3, 4), (5, 8, 3), (3, 1, 5),
+                                            (1000, 4, 1)])
+def test_end_to_end_row_blocks(m, chunks, tail):
+    """end_to_end.HostMatmul's row blocks: contiguous, non-empty, covering [0, m), the
+    last of the ``chunks`` blocks split again (the 8192-row, 8-block, 2-way split
+    that the end-to-end benchmark uses gives two 512-row tail blocks)."""
+    from end_to_end import row_blocks
+
+    blocks = row_blocks(m, chunks, tail)
+    assert blocks[0][0] == 0 and blocks[-1][1] == m
+    assert all(lo < hi for lo, hi in blocks)
+    assert all(blocks[i][1] == blocks[i + 1][0] for i in range(len(blocks) - 1))
+    base = min(chunks, m)
+    last = m - chunk_rows(m, chunks)[-1][0]
+    assert len(blocks) == base - 1 + min(tail, last)
+    if (m, chunks, tail) == (8192, 8, 2):
+        assert blocks[-2:] == [(7168, 7680), (7680, 8192)]
+
+
 def test_plan_peers():
     plan = ShardPlan(64, 8, 8, 4, 2, chunks=2, gather="all")
     assert plan.receivers() == [0, 1, 3] and plan.senders() == [0, 1, 3]
