@@ -114,9 +114,9 @@ int matmul_set_sm_limit(void *context, int sms, char *error, size_t error_size);
 /* No counterpart in the reference.  Same arguments, result and error convention
  * as matmul_launch, for implementation 7 (tcgen05) only, but it never allocates:
  * for callers that must not call cudaMalloc or a stream-ordered allocator --
- * a process whose framework has already reserved nearly all device memory in
- * its own pool, or code that captures a graph in which it may add no memory
- * nodes.  The TF32 rounding copies and the repacked copies of unaligned operands
+ * typically a process whose framework has already reserved nearly all device
+ * memory in its own pool, where one more allocation at launch time would fail
+ * or force that pool to give memory back.  The TF32 rounding copies and the repacked copies of unaligned operands
  * that matmul_launch places in pool memory go instead into one fixed 32 MiB
  * array compiled into the library (every GPU that loads the library holds it
  * until the process exits).  A problem whose copies need more than 32 MiB is

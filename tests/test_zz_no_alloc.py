@@ -1,8 +1,8 @@
 """The allocation-free entry point, matmul_launch_noalloc (needs a B200).
 
 Some callers cannot allocate device memory at call time: their framework has
-already reserved nearly all of it in its own pool, or they capture a graph
-into which no memory nodes may go.  For them the library has a second launch
+already reserved nearly all of it in its own pool, and one more allocation
+would fail or force the pool to give memory back.  For them the library has a second launch
 entry point whose scratch (TF32-rounded and repacked operand copies) lives in
 a fixed 32 MiB array compiled into the library.  These tests call it through
 the C-ABI and check that, on two calls in a row, it gives the same output as
