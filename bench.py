@@ -7,13 +7,15 @@ Metric: device-timed TFLOP/s = 2*M*K*N / t (the reference's src/main.py:102).
 
 * N = 1 (default workload ``square8192``): C = A*B with M=K=N=8192, BF16 inputs
   drawn N(0, 1/sqrt(K)) from a fixed seed, FP32 accumulate and output, through
-  the library's C-ABI (``matmul_launch``, tcgen05 kernel).  A step is one GEMM;
-  W untimed steps, then K steps between CUDA events on the launching stream.
-  A and B (134 MB each) and C (268 MB) are larger than the 126 MB L2, so no
-  flush is needed between steps.  Extra fields report the reference's own
-  timing method (median of 21 CUDA-graph samples of 10 GEMMs after 10 warmups,
-  src/benchmark_backends.py:49-69) for every precision and torch/cuBLAS on the
-  same inputs.
+  the library's C-ABI (``matmul_launch``, tcgen05 kernel), timed the reference's
+  way (src/benchmark_backends.py:49-69): a step is one replay of a CUDA graph of
+  10 GEMMs between external events, captured after 10 eager warm-up GEMMs; W
+  untimed steps, then K timed steps (default 21); value = 2MKN / (median step /
+  10).  A and B (134 MB each) and C (268 MB) are larger than the 126 MB L2, so
+  no flush is needed between steps.  Extra fields: a back-to-back burst of the
+  same launch, the same statistic for every precision beside torch/cuBLAS on the
+  same inputs (replays alternating), the roofline, the CPU baseline and the
+  end-to-end figure through the public API with host buffers.
 * N > 1 (default workload ``rowshard32768``): M=K=N=32768 BF16, U[-1,1), A and C
   row-sharded over the ranks; every step broadcasts one B from rank 0 (posted
   one step ahead on its own communicator, overlapping the GEMMs) and
@@ -64,68 +66,106 @@ def tflops(m, k, n, ms):
 
 # ---------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 100 ms in the background."""
+    """SM clock, power and clock-event reasons of one GPU, sampled every `period`
+    seconds on a background thread through NVML (nvidia-smi's -lms loop when NVML
+    cannot be used); ``summary(t0, t1)`` keeps the samples taken in [t0, t1]."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASON_BITS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+                   "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
+    SMI_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                  "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
-        self.samples = []
-        self.proc = None
-        self.gpu_index = gpu_index
-        self.thread = None
+    def __init__(self, cuda_index: int, period: float = 0.01):
+        self.cuda_index = cuda_index
+        self.period = period
+        self.samples = []          # (time, sm_mhz, max_mhz, power_w, set of reasons)
+        self.source = None
+        self._stop = threading.Event()
+        self._thread = None
+        self._proc = None
 
-    def __enter__(self):
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+
+        pynvml.nvmlInit()
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
-                 "-i", str(self.gpu_index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
-            return self
-        self.thread = threading.Thread(target=self._read, daemon=True)
-        self.thread.start()
-        return self
+            uuid = str(torch.cuda.get_device_properties(self.cuda_index).uuid)
+            return pynvml, pynvml.nvmlDeviceGetHandleByUUID(("GPU-" + uuid).encode())
+        except Exception:
+            visible = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+            ids = [v.strip() for v in visible.split(",") if v.strip()]
+            index = int(ids[self.cuda_index]) if ids and ids[self.cuda_index].isdigit() else self.cuda_index
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(index)
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.samples.append((time.time(), line.strip()))
-
-    def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
+    def _poll_nvml(self, nvml, handle):
+        max_mhz = float(nvml.nvmlDeviceGetMaxClockInfo(handle, nvml.NVML_CLOCK_SM))
+        while not self._stop.is_set():
             try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-            if self.thread is not None:
-                self.thread.join(timeout=5)
+                mhz = float(nvml.nvmlDeviceGetClockInfo(handle, nvml.NVML_CLOCK_SM))
+                power = nvml.nvmlDeviceGetPowerUsage(handle) / 1000.0
+                bits = nvml.nvmlDeviceGetCurrentClocksEventReasons(handle)
+                reasons = {name for name, bit in self.REASON_BITS.items() if bits & bit}
+                self.samples.append((time.time(), mhz, max_mhz, power, reasons))
+            except Exception:
+                pass
+            self._stop.wait(self.period)
 
-    def summary(self, start: float, stop: float) -> dict:
-        rows = [line for t, line in self.samples if start <= t <= stop]
-        window = "timed region"
-        if not rows:
-            rows = [line for _, line in self.samples]
-            window = "whole run"
-        mhz, max_mhz, power, reasons = [], None, [], set()
+    def _poll_smi(self):
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for line in rows:
+        for line in self._proc.stdout:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue
             try:
-                mhz.append(float(parts[1]))
-                max_mhz = float(parts[2])
-                power.append(float(parts[3]))
+                reasons = {name for name, value in zip(names, parts[5:9]) if value.lower() == "active"}
+                self.samples.append((time.time(), float(parts[1]), float(parts[2]), float(parts[3]), reasons))
             except ValueError:
                 continue
-            for name, value in zip(names, parts[5:9]):
-                if value.lower() == "active":
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": max_mhz,
-                "power_w_max": max(power) if power else None, "reasons": sorted(reasons),
-                "samples": len(mhz), "window": window}
+
+    def __enter__(self):
+        try:
+            nvml, handle = self._nvml_handle()
+            self.source = "nvml"
+            self._thread = threading.Thread(target=self._poll_nvml, args=(nvml, handle), daemon=True)
+        except Exception:
+            try:
+                self._proc = subprocess.Popen(
+                    ["nvidia-smi", f"--query-gpu={self.SMI_FIELDS}", "--format=csv,noheader,nounits",
+                     "-lms", str(max(10, int(self.period * 1000))), "-i", str(self.cuda_index)],
+                    stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            except OSError:
+                return self
+            self.source = "nvidia-smi"
+            self._thread = threading.Thread(target=self._poll_smi, daemon=True)
+        self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._proc is not None:
+            self._proc.terminate()
+            try:
+                self._proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self._proc.kill()
+        if self._thread is not None:
+            self._thread.join(timeout=5)
+
+    def summary(self, start: float, stop: float) -> dict:
+        rows = [row for row in self.samples if start <= row[0] <= stop]
+        window = "timed region"
+        if not rows:
+            rows = list(self.samples)
+            window = "whole run"
+        mhz = [row[1] for row in rows]
+        reasons = set().union(*(row[4] for row in rows)) if rows else set()
+        return {"sm_mhz": statistics.median(mhz) if mhz else None,
+                "sm_max_mhz": rows[-1][2] if rows else None,
+                "power_w_max": max(row[3] for row in rows) if rows else None,
+                "reasons": sorted(reasons), "samples": len(rows), "window": window,
+                "window_s": stop - start, "source": self.source}
 
 
 # ---------------------------------------------------------------- reference (CPU) arm
@@ -257,30 +297,47 @@ def single_gpu(args) -> dict:
         run = native.prepare("tcgen05", a, b, c, precision="bf16")
     stream.synchronize()
 
-    # ---- contract timing: W warm-up steps, then K steps between events.
-    with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
-            run()
+    # ---- contract timing, the reference's own statistic (src/benchmark_backends.py:49-69):
+    # one CUDA graph holds DEVICE_BATCH GEMMs between two external events and is
+    # captured after 10 eager warm-up calls; a step is one replay of that graph.  W
+    # untimed replays, then K timed replays between a synchronize on both sides; each
+    # step's device time is its event interval, and value = 2MKN / (median / batch).
+    from benchmark_backends import DEVICE_BATCH
+
+    graph, g_start, g_end = capture_graph_timer(run, stream, warmup=10)
+    for _ in range(args.warmup):
+        graph.replay()
     stream.synchronize()
-    events = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    samples = []
     with ClockSampler(0) as clocks:
-        time.sleep(0.3)
+        time.sleep(0.05)
         torch.cuda.synchronize()
         wall0 = time.time()
-        with torch.cuda.stream(stream):
-            events[0].record(stream)
-            for i in range(args.steps):
-                run()
-                events[i + 1].record(stream)
-        stream.synchronize()
+        for _ in range(args.steps):
+            graph.replay()
+            g_end.synchronize()
+            samples.append(g_start.elapsed_time(g_end))
+        torch.cuda.synchronize()
         wall1 = time.time()
-    per_launch = [events[i].elapsed_time(events[i + 1]) for i in range(args.steps)]
-    total_ms = events[0].elapsed_time(events[-1])
-    ms_per_step = total_ms / args.steps
-    value = tflops(m, k, n, ms_per_step)
-    kernel_ms = statistics.mean(per_launch)
-    achieved = tflops(m, k, n, kernel_ms)
+    ms_per_step = statistics.median(samples)
+    kernel_ms = ms_per_step / DEVICE_BATCH
+    value = tflops(m, k, n, kernel_ms)
+    achieved = value
     clock_summary = clocks.summary(wall0, wall1)
+    del graph
+
+    # ---- the same kernel as a burst: back-to-back launches between two events (no graph).
+    burst_launches = 100
+    b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        b0.record(stream)
+        for _ in range(burst_launches):
+            run()
+        b1.record(stream)
+    stream.synchronize()
+    burst_ms = b0.elapsed_time(b1) / burst_launches
+    burst = {"launches": burst_launches, "mean_ms": burst_ms, "tflops": tflops(m, k, n, burst_ms),
+             "timing": "back-to-back launches between two CUDA events on the launching stream"}
     status = native.device_status()
 
     # ---- correctness cross-check against torch/cuBLAS on the same inputs (not an oracle).
@@ -364,16 +421,24 @@ def single_gpu(args) -> dict:
         "data": "synthetic: A, B ~ N(0, 1/sqrt(K)) from a fixed seed, rounded to BF16 (RNE)",
         "config": {"workload": "gemm_bf16_8192x8192x8192", "m": m, "k": k, "n": n, "precision": "bf16",
                    "backend": "tcgen05 (matmul_launch impl 7)", "output": "FP32 row-major",
+                   "step": f"one replay of a CUDA graph of {DEVICE_BATCH} GEMMs between external events "
+                           "(the reference's measure_cuda_device); value = 2MKN / (median step / "
+                           f"{DEVICE_BATCH}), after 10 eager warm-up GEMMs and W warm-up replays",
+                   "gemms_per_step": DEVICE_BATCH,
                    "l2": "inputs larger than L2 (A, B 134 MB each, C 268 MB > 126 MB L2); no flush",
                    "parallelism": "single GPU"},
+        "step_ms": {"median": ms_per_step, "min": min(samples), "max": max(samples),
+                    "mean": statistics.mean(samples)},
+        "burst": burst,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "traffic": traffic,
                      "peak_source": f"{peak_kind} bf16_tflops (burst, cuBLAS 8192^3)",
                      "kernel": f"{plan['kernel']} {plan['tile_m']}x{plan['tile_n']} BF16", "kernel_ms": kernel_ms,
+                     "kernel_ms_source": "median graph step / GEMMs per step (CUDA events on the launching stream)",
                      "algorithmic_flops_per_launch": 2.0 * m * k * n},
         "cpu_baseline": cpu_baseline(),
         "e2e": e2e,
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * DEVICE_BATCH,
         "clocks": clock_summary,
         "check": check,
         "per_precision": per_precision,
@@ -486,9 +551,11 @@ def main() -> int:
                         help="multi-GPU: SMs left free of GEMM CTAs for the NCCL kernels that overlap them")
     parser.add_argument("--gather", choices=("all", "root"), default="all")
     parser.add_argument("--quick", action="store_true", help="skip the per-precision and cuBLAS tables")
-    parser.add_argument("--sweep", choices=("square", "llm", "ragged", "all"), default=None,
+    parser.add_argument("--sweep", choices=("square", "llm", "ragged", "all", "legacy"), default=None,
                         help="instead of the contract line, time every shape of a configuration "
-                             "(reference graph method, one JSON line per case, torch/cuBLAS beside it)")
+                             "(reference graph method, one JSON line per case, torch/cuBLAS beside it); "
+                             "'legacy' times the reference's own kernels (oracle/_ref/matmul.so) at "
+                             "4096^3 and 8192^3 as comparison rows")
     parser.add_argument("--cases", nargs="+", default=None, metavar="MxKxN:PREC[:normal]",
                         help="like --sweep, for the listed shapes (inputs U[-1,1), or N(0, 1/sqrt(K)) with :normal)")
     args = parser.parse_args()
@@ -500,7 +567,10 @@ def main() -> int:
     if args.workload is None:
         args.workload = "square8192" if args.gpus == 1 else "rowshard32768"
     if args.steps is None:
-        args.steps = 500 if args.workload == "square8192" else 20
+        args.steps = 21 if args.workload == "square8192" else 20
+    if args.sweep == "legacy":
+        legacy_sweep()
+        return 0
     if args.sweep or args.cases:
         sweep(args.sweep, [parse_case(text) for text in args.cases] if args.cases else None)
         return 0
@@ -592,6 +662,8 @@ def sweep(which: str | None, explicit: list | None = None) -> None:
         del ours_timer, theirs_timer
         stream.synchronize()
         diff = float((c - ref).abs().max().item())
+        with torch.cuda.stream(stream):
+            check_ratio, check_err = native.check_fp64(a, b, c, precision)
         bytes_min = (4 if precision in ("fp32", "tf32") else 2) * (m * k + k * n) + 4 * m * n
         line = {"case": f"{m}x{k}x{n}", "precision": precision, "backend": backend,
                 "median_ms": ours["median_ms"], "tflops": ours["tflops"],
@@ -599,12 +671,109 @@ def sweep(which: str | None, explicit: list | None = None) -> None:
                 "frac_bf16_peak": ours["tflops"] / peaks["bf16_tflops"],
                 "torch_cublas_tflops": theirs["tflops"], "ratio_vs_cublas": ours["tflops"] / theirs["tflops"],
                 "max_abs_diff_vs_cublas": diff, "inputs": dist,
+                "check_fp64_ratio": check_ratio, "check_fp64_max_abs_err": check_err,
+                "check": "matmul_check_fp64 over every output (FP64 product of the rounded inputs, "
+                         "the reference's GemmReference allowance; <= 1 passes)",
                 "timing": "reference graph method (median of 21 replays of 10 GEMMs after 10 warmups), "
                           "replays alternating with cuBLAS's"}
         print(json.dumps(line), flush=True)
         del a, b, c, ref, run
     status = native.device_status()
     native.close()
+    if status:
+        raise RuntimeError(f"device status {status:#x}")
+
+
+LEGACY_IMPLEMENTATIONS = {"fp32": ((2, "cublas"), (4, "warp_large"), (5, "pipeline")),
+                          "tf32": ((2, "cublas"), (6, "wmma")), "fp16": ((2, "cublas"), (6, "wmma")),
+                          "bf16": ((2, "cublas"), (6, "wmma"))}
+
+
+def legacy_sweep(sizes=(4096, 8192)) -> None:
+    """Comparison rows: the reference's own CUDA library (its src/matmul.cu built
+    unmodified for sm_100a into oracle/_ref/matmul.so) -- its cuBLAS branch, its
+    cp.async FP32 kernels and its wmma tensor-core kernel (src/matmul.cu:401-474)
+    -- timed with the same graph method and inputs as this library, whose row is
+    printed beside each.  These rows measure the reference's kernels, not this
+    library; every output is checked by matmul_check_fp64."""
+    import ctypes
+
+    import torch
+
+    from gpumat import NativeMatmul
+    from precision import INPUT_DTYPES, torch_precision
+
+    path = ROOT / "oracle" / "_ref" / "matmul.so"
+    if not path.exists():
+        print(json.dumps({"legacy": "unavailable", "why": f"{path} not built (make -C oracle ref)"}), flush=True)
+        return
+    ref = ctypes.CDLL(str(path))
+    ref.matmul_create.restype = ctypes.c_void_p
+    ref.matmul_create.argtypes = [ctypes.c_int, ctypes.c_char_p, ctypes.c_size_t]
+    ref.matmul_destroy.argtypes = [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_size_t]
+    ref.matmul_launch.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
+                                  ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                                  ctypes.c_char_p, ctypes.c_size_t]
+    err = ctypes.create_string_buffer(1024)
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    ref_ctx = ref.matmul_create(0, err, len(err))
+    if not ref_ctx:
+        raise RuntimeError(f"reference matmul_create failed: {err.value.decode()}")
+    native = NativeMatmul(device=0)
+    stream = torch.cuda.Stream(device=device)
+    precision_ids = {"fp32": 0, "tf32": 1, "fp16": 2, "bf16": 3}
+    for size in sizes:
+        m = k = n = size
+        for precision, impls in LEGACY_IMPLEMENTATIONS.items():
+            dtype = getattr(torch, INPUT_DTYPES[precision])
+            gen = torch.Generator(device=device)
+            gen.manual_seed(size + len(precision))
+            with torch.cuda.stream(stream):
+                a32 = torch.rand((m, k), generator=gen, device=device) * 2 - 1
+                b32 = torch.rand((k, n), generator=gen, device=device) * 2 - 1
+                a = torch.empty((m, k), dtype=dtype, device=device)
+                b = torch.empty((k, n), dtype=dtype, device=device)
+                native.convert(a32, a, precision)
+                native.convert(b32, b, precision)
+                del a32, b32
+                c = torch.empty((m, n), dtype=torch.float32, device=device)
+                ours = native.prepare("ffma" if precision == "fp32" else "tcgen05", a, b, c, precision=precision)
+            stream_ptr = ctypes.c_void_p(stream.cuda_stream)
+
+            def legacy_call(impl):
+                def call():
+                    if ref.matmul_launch(ref_ctx, impl, precision_ids[precision], ctypes.c_void_p(a.data_ptr()),
+                                         ctypes.c_void_p(b.data_ptr()), ctypes.c_void_p(c.data_ptr()), m, k, n,
+                                         stream_ptr, err, len(err)) != 0:
+                        raise RuntimeError(f"reference matmul_launch failed: {err.value.decode()}")
+                return call
+
+            timers = [capture_graph_timer(ours, stream)]
+            names = ["b200 (this library)"]
+            with torch_precision(torch, precision):
+                for impl, name in impls:
+                    timers.append(capture_graph_timer(legacy_call(impl), stream))
+                    names.append(f"reference {name} (impl {impl})")
+            results = interleaved_reference_method(timers, m, k, n)
+            del timers
+            for (impl_name, result), impl in zip(zip(names, results), [None] + [i for i, _ in impls]):
+                with torch.cuda.stream(stream):
+                    if impl is None:
+                        ours()
+                    else:
+                        legacy_call(impl)()
+                    ratio, max_err = native.check_fp64(a, b, c, precision)
+                print(json.dumps({"case": f"{m}x{k}x{n}", "precision": precision, "implementation": impl_name,
+                                  "median_ms": result["median_ms"], "tflops": result["tflops"],
+                                  "check_fp64_ratio": ratio, "check_fp64_max_abs_err": max_err,
+                                  "timing": "reference graph method (median of 21 replays of 10 GEMMs after 10 "
+                                            "warmups), replays of all rows of the case alternating",
+                                  "inputs": "U[-1,1) rounded to the input precision"}), flush=True)
+            del a, b, c, ours
+    status = native.device_status()
+    native.close()
+    ref.matmul_destroy(ref_ctx, err, len(err))
     if status:
         raise RuntimeError(f"device status {status:#x}")
 

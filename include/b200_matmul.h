@@ -111,6 +111,19 @@ int matmul_plan(void *context, int implementation, int precision, int m, int k, 
  * launches from other threads on the same context. */
 int matmul_set_sm_limit(void *context, int sms, char *error, size_t error_size);
 
+/* No counterpart in the reference (whose kernels have no waits that can run
+ * out; its error convention is src/matmul.cu:36-47, launch errors :475-478).
+ * Sets the limit, in nanoseconds of GPU time, of the tensor-core kernels'
+ * progress waits (a stage to land, an accumulator to fill or to be read) for
+ * later launches of this context; 0 restores the default of 2 s, larger values
+ * are rejected.  Waits for copies and MMAs already issued keep 2 s.  When a
+ * progress wait runs out the kernel sets bits of the device status word (see
+ * matmul_device_status), writes NaN over every output element it did not
+ * finish, releases its tensor memory and returns, so that the context stays
+ * usable and an FP64 check of C fails.  For watchdog tests and for callers that
+ * want a kernel to give up sooner; the FFMA kernels have no such waits. */
+int matmul_set_wait_limit(void *context, unsigned long long nanoseconds, char *error, size_t error_size);
+
 /* No counterpart in the reference.  Same arguments, result and error convention
  * as matmul_launch, for implementation 7 (tcgen05) only, but it never allocates:
  * for callers that must not call cudaMalloc or a stream-ordered allocator --
@@ -121,13 +134,20 @@ int matmul_set_sm_limit(void *context, int sms, char *error, size_t error_size);
  * array compiled into the library (every GPU that loads the library holds it
  * until the process exits).  A problem whose copies need more than 32 MiB is
  * rejected with "matmul_launch_noalloc: this problem needs N bytes of scratch,
- * more than the fixed ..." (TF32 above m*k*n = 2^25 needs 4*(m*k' + n*k') bytes
- * with k' = k rounded up to 4; smaller TF32 problems, split-K launches and
- * aligned BF16/FP16 operands need none).  The first call on a
- * device looks up the array's device address with that device current; make
- * that first call before any stream capture.  All calls share the one array and
- * every call rewrites the part it uses, so calls that overlap on the GPU (other
- * streams, or other threads) race: order them on one stream. */
+ * more than the fixed ...".  The rule is the one matmul_launch applies, whatever
+ * kernel the launch plan then picks (split K included): a TF32 problem with
+ * m*k*n > 2^25 copies both operands, 4*m*k' + 4*n*k' bytes with k' = k rounded
+ * up to 4; an FP16/BF16 operand whose base address is not 16-byte aligned, or
+ * whose row pitch (2*k bytes for A, 2*n for B) is not a multiple of 16, is
+ * repacked into m*k'' (A) or k*n'' (B) 2-byte elements with k'', n'' rounded up
+ * to 8; each copy is rounded up to 256 bytes.  TF32 problems with m*k*n <= 2^25
+ * and aligned FP16/BF16 operands need no scratch.  The first call through a
+ * context looks up the array's device address with that context's device
+ * current and keeps it in the context; make that first call before any stream
+ * capture (a context does not survive a device reset; create a new one after
+ * it).  All calls share the one array and every call rewrites the part it uses,
+ * so calls that overlap on the GPU (other streams, or other threads) race:
+ * order them on one stream. */
 int matmul_launch_noalloc(void *context, int implementation, int precision,
                           const void *a, const void *b, float *c, int m, int k, int n,
                           void *stream, char *error, size_t error_size);

@@ -34,29 +34,6 @@ namespace {
 
 using namespace b200;
 
-// Device address of g_noalloc_scratch per device, looked up once per device with
-// that device current.  In host code the symbol itself is only a host-side
-// stand-in, never a device address.
-constexpr int kMaxDevices = 64;
-std::mutex g_noalloc_mutex;
-void *g_noalloc_address[kMaxDevices] = {};
-
-cudaError_t noalloc_scratch_address(int device, void **address)
-{
-    if (device < 0 || device >= kMaxDevices)
-        return cudaErrorInvalidDevice;
-    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-    if (!g_noalloc_address[device]) {
-        void *ptr = nullptr;
-        const cudaError_t st = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
-        if (st != cudaSuccess)
-            return st;
-        g_noalloc_address[device] = ptr;
-    }
-    *address = g_noalloc_address[device];
-    return cudaSuccess;
-}
-
 constexpr int kAbiVersion = 3;
 constexpr int kImplTcgen05 = 7;
 constexpr int kImplFfma = 8;
@@ -85,7 +62,36 @@ struct Context {
     int ffma_resident[2] = {}; // resident blocks per SM of each aligned FFMA tile
     EncodeTiledFn encode = nullptr;
     cudaMemPool_t pool = nullptr;
+    // Device address of g_noalloc_scratch in this context's device, looked up by
+    // the context's first matmul_launch_noalloc call with the device current (in
+    // host code the symbol itself is a host-side stand-in, never a device
+    // address).  Kept per context, so a context created after a device reset
+    // looks it up again in the reloaded module.
+    std::mutex noalloc_mutex;
+    void *noalloc_scratch = nullptr;
+    // Limit of the bounded waits that depend on another warp's progress
+    // (matmul_set_wait_limit); 0 = the default.
+    unsigned long long wait_limit_ns = 0;
 };
+
+unsigned long long wait_limit(const Context *ctx)
+{
+    return ctx->wait_limit_ns ? ctx->wait_limit_ns : kWaitLimitNs;
+}
+
+cudaError_t noalloc_scratch_address(Context *ctx, void **address)
+{
+    std::lock_guard<std::mutex> lock(ctx->noalloc_mutex);
+    if (!ctx->noalloc_scratch) {
+        void *ptr = nullptr;
+        const cudaError_t st = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+        if (st != cudaSuccess)
+            return st;
+        ctx->noalloc_scratch = ptr;
+    }
+    *address = ctx->noalloc_scratch;
+    return cudaSuccess;
+}
 
 void clear_error(char *error, size_t error_size)
 {
@@ -430,6 +436,7 @@ int launch_skinny(Context *ctx, int prec, const void *a_op, int64_t lda, const v
     const int splits = skinny_splits(ctx, n, params.total_k_blocks);
     params.num_k_blocks = (params.total_k_blocks + splits - 1) / splits;
     params.c = c;
+    params.wait_limit_ns = wait_limit(ctx);
     // Split K: one 128-column slab per cluster of `splits` CTAs along z.
     const dim3 grid = splits > 1 ? dim3(static_cast<unsigned int>(params.num_n_tiles), 1,
                                         static_cast<unsigned int>(splits))
@@ -574,6 +581,7 @@ int launch_tcgen05(Context *ctx, int prec, const void *a, const void *b, float *
     params.c = c;
     params.c_direct = c_direct ? 1 : 0;
     params.a_box_rows = a_box_rows;
+    params.wait_limit_ns = wait_limit(ctx);
     const int units = pair ? ctx->max_pairs : ctx->sm_count;
     const int grid = static_cast<int>(tiles < units ? tiles : units) * (pair ? 2 : 1);
 
@@ -1147,6 +1155,17 @@ extern "C" int matmul_set_sm_limit(void *opaque, int sms, char *error, size_t er
     return 0;
 }
 
+extern "C" int matmul_set_wait_limit(void *opaque, unsigned long long nanoseconds, char *error, size_t error_size)
+{
+    clear_error(error, error_size);
+    if (!opaque)
+        return fail(error, error_size, "matmul_set_wait_limit", "context is null");
+    if (nanoseconds > kWaitLimitNs)
+        return fail(error, error_size, "matmul_set_wait_limit", "the limit cannot exceed 2 s (2000000000 ns)");
+    static_cast<Context *>(opaque)->wait_limit_ns = nanoseconds;
+    return 0;
+}
+
 extern "C" int matmul_convert(void *opaque, int precision, const float *src, void *dst, size_t count, void *stream,
                               char *error, size_t error_size)
 {
@@ -1230,7 +1249,7 @@ extern "C" int matmul_launch_noalloc(void *opaque, int implementation, int preci
     if (st != cudaSuccess)
         return fail_cuda(error, error_size, "cudaSetDevice", st);
     void *scratch = nullptr;
-    st = noalloc_scratch_address(ctx->device, &scratch);
+    st = noalloc_scratch_address(ctx, &scratch);
     if (st != cudaSuccess)
         return fail_cuda(error, error_size, "matmul_launch_noalloc: cudaGetSymbolAddress", st);
     return launch_tcgen05(ctx, precision, a, b, c, m, k, n, static_cast<cudaStream_t>(stream), error, error_size,

@@ -2,8 +2,14 @@
 // tcgen05 (TMEM allocation, MMA, commit, loads) and proxy fences.
 //
 // Every wait on an mbarrier goes through mbar_wait(), which polls with
-// try_wait and gives up after kWaitLimitNs of %globaltimer time so that a
-// protocol error ends the kernel with a status flag instead of hanging the GPU.
+// try_wait and gives up after a limit of %globaltimer time so that a protocol
+// error ends the kernel with a status flag instead of hanging the GPU.  Two
+// kinds of wait:
+//   * progress waits (a stage to land, an accumulator to fill or drain) use
+//     the launch's limit, kWaitLimitNs unless matmul_set_wait_limit lowered it;
+//   * drain waits (copies and MMAs this CTA or its pair has already issued,
+//     which always complete) keep kWaitLimitNs, so that no CTA can leave while
+//     a copy into its shared memory or an MMA on its TMEM is still in flight.
 #pragma once
 
 #include <cstdint>
@@ -80,18 +86,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity)
 }
 
 // Waits until the phase with the given parity has completed.  Returns false
-// (without waiting further) once kWaitLimitNs has passed.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity)
+// (without waiting further) once `limit_ns` has passed.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint64_t limit_ns = kWaitLimitNs)
 {
     if (mbar_try_wait(bar, parity))
         return true;
+    // try_wait itself suspends the thread for a while before it reports "not yet",
+    // so reading the timer after every poll costs nothing that matters and keeps
+    // a short limit honoured.
     const uint64_t start = global_timer_ns();
     for (;;) {
-#pragma unroll 1
-        for (int i = 0; i < 32; ++i)
-            if (mbar_try_wait(bar, parity))
-                return true;
-        if (global_timer_ns() - start > kWaitLimitNs)
+        if (mbar_try_wait(bar, parity))
+            return true;
+        if (global_timer_ns() - start > limit_ns)
             return false;
     }
 }
@@ -284,6 +291,14 @@ __device__ __forceinline__ float4 ld_shared_cluster_f4(uint32_t cluster_addr)
                  : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
                  : "r"(cluster_addr)
                  : "memory");
+    return v;
+}
+
+// 4-byte load from the shared memory of a CTA of this cluster (a mapa address).
+__device__ __forceinline__ uint32_t ld_shared_cluster_u32(uint32_t cluster_addr)
+{
+    uint32_t v;
+    asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(cluster_addr) : "memory");
     return v;
 }
 

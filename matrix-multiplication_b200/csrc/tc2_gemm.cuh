@@ -24,7 +24,10 @@
 // epilogue has read those columns too.  The K order of every sum is unchanged,
 // so both widths give the same bits (1-3 deferred blocks measured alike).
 //
-// Synchronisation (all waits bounded, see ptx.cuh):
+// Synchronisation (all waits bounded, see ptx.cuh; the producers' waits for a
+// freed stage keep the fixed limit, so that when the MMA thread gives up both
+// CTAs of the pair stop issuing at the same stage and the leader's drain of its
+// full barriers covers every copy either CTA issued):
 //   full[s]   leader only; the leader's producer arms it with both CTAs' bytes,
 //             both CTAs' TMA loads complete on it (cta_group::2 loads).
 //   empty[s]  in both CTAs; one multicast tcgen05.commit from the leader's MMA
@@ -220,7 +223,7 @@ tc2_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
             uint32_t acc_phase = 0;
             bool ok = true;
             for (int tile = pair; ok && tile < p.num_tiles; tile += pairs) {
-                if (!mbar_wait(acce_bar(acc), acc_phase ^ 1u)) {
+                if (!mbar_wait(acce_bar(acc), acc_phase ^ 1u, p.wait_limit_ns)) {
                     report_status(kStatusMmaTimeout);
                     break;
                 }
@@ -230,7 +233,7 @@ tc2_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
                 bool upper_live = false;              // BN = 512: the epilogue has read columns 256-511
                 int pending = 0, pending_stage = 0;   // BN = 512: K blocks whose column 256-511 MMAs wait
                 for (int kb = 0; kb < nkb; ++kb) {
-                    if (!mbar_wait(full_bar(stage), phase)) {
+                    if (!mbar_wait(full_bar(stage), phase, p.wait_limit_ns)) {
                         report_status(kStatusMmaTimeout);
                         ok = false;
                         break;
@@ -255,7 +258,7 @@ tc2_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
                                 pending_stage = stage;
                             if (kb == nkb - 1 || (!upper_live && kb == kDefer - 1)) {
                                 if (!upper_live) {
-                                    if (!mbar_wait(acce_bar(1), acc_phase ^ 1u)) {
+                                    if (!mbar_wait(acce_bar(1), acc_phase ^ 1u, p.wait_limit_ns)) {
                                         report_status(kStatusMmaTimeout);
                                         ok = false;
                                         break;
@@ -302,7 +305,7 @@ tc2_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
         auto wait_accf = [&](int i) {
             int ok = 1;
             if (lane == 0)
-                ok = mbar_wait(accf_bar(i), acc_phase) ? 1 : 0;
+                ok = mbar_wait(accf_bar(i), acc_phase, p.wait_limit_ns) ? 1 : 0;
             ok = epilogue_all(__shfl_sync(0xffffffffu, ok, 0));
             if (!ok && lane == 0)
                 report_status(kStatusEpilogueTimeout);
@@ -310,18 +313,23 @@ tc2_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
             return ok != 0;
         };
         bool ok = true;
+        int failed_tile = -1;     // the first tile not finished (the same in all four warps)
         for (int tile = pair; ok && tile < p.num_tiles; tile += pairs) {
             int mb, nb;
             tc_tile_coords(tile, p, mb, nb);
-            if (!wait_accf(kAccs == 2 ? acc : 0))
+            if (!wait_accf(kAccs == 2 ? acc : 0)) {
+                failed_tile = tile;
                 break;
+            }
             const int tile_row0 = mb * TC2_BM + static_cast<int>(rank) * TC2_HALF;   // first row of this CTA's part of the tile
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                    static_cast<uint32_t>(acc * BN);
 #pragma unroll 1
             for (int chunk = 0; chunk < BN / 32; ++chunk) {
-                if (kAccs == 1 && chunk == 8 && !(ok = wait_accf(1)))     // BN = 512: columns 256-511
+                if (kAccs == 1 && chunk == 8 && !(ok = wait_accf(1))) {   // BN = 512: columns 256-511
+                    failed_tile = tile;
                     break;
+                }
                 uint32_t v[32];
                 tmem_load_32cols(t_row + chunk * 32, v);
                 if (chunk % 8 == 7) {
@@ -383,9 +391,23 @@ tc2_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
                 acc_phase ^= 1u;
             }
         }
-        if (warp == 2 && lane == 0)
-            bulk_wait_group_read<0>();     // shared memory free; the writes complete with the grid
+        if (warp == 2 && lane == 0) {
+            if (failed_tile >= 0)
+                bulk_wait_group<0>();      // the stored boxes are in C before the NaN below
+            else
+                bulk_wait_group_read<0>(); // shared memory free; the writes complete with the grid
+        }
         __syncwarp();
+        if (failed_tile >= 0) {
+            // This CTA's rows of every tile from the first unfinished one on.
+            epilogue_sync();
+            for (int tile = failed_tile; tile < p.num_tiles; tile += pairs) {
+                int mb, nb;
+                tc_tile_coords(tile, p, mb, nb);
+                fill_nan(p.c, p.m, p.n, mb * TC2_BM + static_cast<int>(rank) * TC2_HALF, TC2_HALF, nb * BN, BN,
+                         quarter, 4, lane);
+            }
+        }
     }
 
     // Neither CTA releases TMEM before the pair's last MMA and both epilogues are done.

@@ -60,6 +60,31 @@ __device__ __forceinline__ void report_status(unsigned int flag)
     atomicOr(&g_device_status, flag);
 }
 
+// A kernel whose progress wait ran out writes NaN over every output element it
+// did not finish, so that a later FP64 check of C fails loudly instead of
+// passing over stale values: rows [row0, row0 + rows) x columns [col0, col0 +
+// cols) of C, clipped to m x n, one warp per row (lanes along the columns).
+__device__ __forceinline__ void fill_nan(float *c, int m, int n, int row0, int rows, int col0, int cols,
+                                         int warp_index, int warps, int lane)
+{
+    const int row_end = min(m, row0 + rows), col_end = min(n, col0 + cols);
+    const float nan = __int_as_float(0x7fc00000);
+    for (int r = row0 + warp_index; r < row_end; r += warps)
+        for (int col = col0 + lane; col < col_end; col += 32)
+            c[static_cast<size_t>(r) * n + col] = nan;
+}
+
+// Whether any CTA of this cluster (ranks 0 .. ctas-1) set its failure flag (a
+// 32-bit word at the same shared-memory offset in every CTA).  Only between two
+// cluster barriers, while every CTA of the cluster is still running.
+__device__ __forceinline__ bool cluster_any_failed(uint32_t flag, int ctas)
+{
+    uint32_t any = 0;
+    for (int r = 0; r < ctas; ++r)
+        any |= ld_shared_cluster_u32(map_to_cta(flag, static_cast<uint32_t>(r)));
+    return any != 0;
+}
+
 enum TcFormat : int { kFmtF16 = 0, kFmtBF16 = 1, kFmtTF32 = 2 };
 
 constexpr int TC_BM = 128;                  // rows per tile (TMEM lanes)
@@ -100,6 +125,7 @@ struct TcParams {
     float *c;        // output (direct-store epilogue only)
     int c_direct;    // 1 when C cannot be written by TMA
     int a_box_rows;  // rows per A box (single-CTA kernel: m rounded up to 16 when m < 128)
+    unsigned long long wait_limit_ns;   // limit of the progress waits (ptx.cuh)
 };
 
 // Instruction descriptor (kind::f16 / kind::tf32): FP32 accumulator (bits 4-5 = 1),
@@ -162,7 +188,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     const uint32_t drain_bar = s_bar + 8u * (2 * kStages + 4);
     const uint32_t tmem_slot = s_bar + 8u * (2 * kStages + 5);
     const uint32_t recv_bar = s_bar + 8u * (2 * kStages + 6);   // split K: partial slices received
+    const uint32_t fail_flag = s_bar + 8u * (2 * kStages + 7);  // 1 once a progress wait of this CTA ran out
     uint32_t *tmem_slot_ptr = reinterpret_cast<uint32_t *>(smem_raw + (tmem_slot - raw));
+    volatile uint32_t *fail_flag_ptr = reinterpret_cast<volatile uint32_t *>(smem_raw + (fail_flag - raw));
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -184,6 +212,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         }
         mbar_init(drain_bar, 1);
         mbar_init(recv_bar, 1);
+        *fail_flag_ptr = 0u;
         fence_mbarrier_init();
     }
     if (warp == 0 && lane == 0) {
@@ -214,7 +243,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 int mb, nb;
                 tc_tile_coords(tile, p, mb, nb);
                 for (int kb = kb_begin; kb < kb_end; ++kb) {
-                    if (!mbar_wait(empty_bar(stage), phase ^ 1u)) {
+                    if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.wait_limit_ns)) {
                         report_status(kStatusLoadTimeout);
                         ok = false;
                         break;
@@ -262,14 +291,14 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             uint32_t acc_phase = 0;
             bool ok = true;
             for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
-                if (!mbar_wait(acce_bar(acc), acc_phase ^ 1u)) {
+                if (!mbar_wait(acce_bar(acc), acc_phase ^ 1u, p.wait_limit_ns)) {
                     report_status(kStatusMmaTimeout);
                     break;
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
                 for (int kb = kb_begin; kb < kb_end; ++kb) {
-                    if (!mbar_wait(full_bar(stage), phase)) {
+                    if (!mbar_wait(full_bar(stage), phase, p.wait_limit_ns)) {
                         report_status(kStatusMmaTimeout);
                         ok = false;
                         break;
@@ -310,16 +339,20 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         int acc = 0;
         uint32_t acc_phase = 0;
         uint32_t stores = 0;
+        int failed_tile = -1;     // the first tile whose accumulator never arrived (the same in all four warps)
         for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
             int mb, nb;
             tc_tile_coords(tile, p, mb, nb);
             int ok = 1;
             if (lane == 0)
-                ok = mbar_wait(accf_bar(acc), acc_phase) ? 1 : 0;
+                ok = mbar_wait(accf_bar(acc), acc_phase, p.wait_limit_ns) ? 1 : 0;
             ok = epilogue_all(__shfl_sync(0xffffffffu, ok, 0));
             if (!ok) {
-                if (lane == 0)
+                if (lane == 0) {
                     report_status(kStatusEpilogueTimeout);
+                    *fail_flag_ptr = 1u;
+                }
+                failed_tile = tile;
                 break;
             }
             tc_fence_after();
@@ -388,9 +421,21 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 acc_phase ^= 1u;
             }
         }
-        if (warp == 2 && lane == 0)
-            bulk_wait_group_read<0>();     // shared memory free; the writes complete with the grid
+        if (warp == 2 && lane == 0) {
+            if (failed_tile >= 0)
+                bulk_wait_group<0>();      // the stored boxes are in C before the NaN below
+            else
+                bulk_wait_group_read<0>(); // shared memory free; the writes complete with the grid
+        }
         __syncwarp();
+        if (failed_tile >= 0 && splits == 1) {
+            epilogue_sync();
+            for (int tile = failed_tile; tile < p.num_tiles; tile += gridDim.x) {
+                int mb, nb;
+                tc_tile_coords(tile, p, mb, nb);
+                fill_nan(p.c, p.m, p.n, mb * TC_BM, TC_BM, nb * BN, BN, quarter, 4, lane);
+            }
+        }
     }
 
     if (splits > 1 && kPartialBytes + static_cast<uint32_t>(splits - 1) * (kPartialBytes / splits) >
@@ -410,6 +455,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         if (threadIdx.x == 0)
             mbar_arrive_expect_tx(recv_bar, static_cast<uint32_t>(splits - 1) * slice_bytes);
         cluster_sync_all();     // every CTA of the cluster is past its main loop: rings idle
+        // A CTA whose progress wait ran out has no valid partial: the rows of
+        // every CTA of the cluster become NaN.
+        const bool any_failed = cluster_any_failed(fail_flag, splits);
         if (warp >= 2) {
             const int quarter = warp & 3;
             const int r = quarter * 32 + lane;
@@ -448,12 +496,14 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             received = mbar_wait(recv_bar, 0) ? 1 : 0;
         received = __shfl_sync(0xffffffffu, received, 0);
         if (!received && lane == 0)
-            report_status(kStatusEpilogueTimeout);
+            report_status(kStatusDrainTimeout);
         int mb, nb;
         tc_tile_coords(static_cast<int>(blockIdx.x), p, mb, nb);
+        if (any_failed || !received)
+            fill_nan(p.c, p.m, p.n, mb * TC_BM + z * rows, rows, nb * BN, BN, warp, TC_THREADS / 32, lane);
         const bool vec = !p.c_direct;
         const uint8_t *ring = smem_raw + (s_a - raw);
-        for (int idx = threadIdx.x; received && idx < rows * (BN / 4); idx += TC_THREADS) {
+        for (int idx = threadIdx.x; received && !any_failed && idx < rows * (BN / 4); idx += TC_THREADS) {
             const int rl = idx / (BN / 4), q = idx % (BN / 4);
             const int r = z * rows + rl;                       // row within the tile
             const uint32_t offset = static_cast<uint32_t>(rl) * kPartialRowBytes +

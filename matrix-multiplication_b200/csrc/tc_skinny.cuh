@@ -47,6 +47,7 @@ struct SkParams {
     int num_k_blocks;         // K blocks per split (all of them when gridDim.z == 1)
     int total_k_blocks;
     float *c;
+    unsigned long long wait_limit_ns;   // limit of the progress waits (ptx.cuh)
 };
 
 template <int FMT, int NP>
@@ -85,7 +86,9 @@ tc_skinny_kernel(const __grid_constant__ CUtensorMap map_bt, const __grid_consta
     const uint32_t drain_bar = s_bar + 8u * (2 * kStages + 4);
     const uint32_t tmem_slot = s_bar + 8u * (2 * kStages + 5);
     const uint32_t recv_bar = s_bar + 8u * (2 * kStages + 6);   // split K: partial rows received
+    const uint32_t fail_flag = s_bar + 8u * (2 * kStages + 7);  // 1 once a progress wait of this CTA ran out
     uint32_t *tmem_slot_ptr = reinterpret_cast<uint32_t *>(smem_raw + (tmem_slot - raw));
+    volatile uint32_t *fail_flag_ptr = reinterpret_cast<volatile uint32_t *>(smem_raw + (fail_flag - raw));
     // Split K: 128 x NP FP32 partial rows (n) padded to NP + 4 floats, then the
     // S-1 received slices, in the idle operand ring.
     constexpr uint32_t kPartialPitch = (NP + 4) * 4;
@@ -109,6 +112,7 @@ tc_skinny_kernel(const __grid_constant__ CUtensorMap map_bt, const __grid_consta
         }
         mbar_init(drain_bar, 1);
         mbar_init(recv_bar, 1);
+        *fail_flag_ptr = 0u;
         fence_mbarrier_init();
     }
     if (warp == 0 && lane == 0) {
@@ -135,7 +139,7 @@ tc_skinny_kernel(const __grid_constant__ CUtensorMap map_bt, const __grid_consta
             bool ok = true;
             for (int nt = blockIdx.x; ok && nt < p.num_n_tiles; nt += gridDim.x) {
                 for (int kb = kb0; kb < kb1; ++kb) {
-                    if (!mbar_wait(empty_bar(stage), phase ^ 1u)) {
+                    if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.wait_limit_ns)) {
                         report_status(kStatusLoadTimeout);
                         ok = false;
                         break;
@@ -179,14 +183,14 @@ tc_skinny_kernel(const __grid_constant__ CUtensorMap map_bt, const __grid_consta
             uint32_t acc_phase = 0;
             bool ok = true;
             for (int nt = blockIdx.x; ok && nt < p.num_n_tiles; nt += gridDim.x) {
-                if (!mbar_wait(acce_bar(acc), acc_phase ^ 1u)) {
+                if (!mbar_wait(acce_bar(acc), acc_phase ^ 1u, p.wait_limit_ns)) {
                     report_status(kStatusMmaTimeout);
                     break;
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * NP);
                 for (int kb = kb0; kb < kb1; ++kb) {
-                    if (!mbar_wait(full_bar(stage), phase)) {
+                    if (!mbar_wait(full_bar(stage), phase, p.wait_limit_ns)) {
                         report_status(kStatusMmaTimeout);
                         ok = false;
                         break;
@@ -225,14 +229,18 @@ tc_skinny_kernel(const __grid_constant__ CUtensorMap map_bt, const __grid_consta
         const int quarter = warp & 3;                 // TMEM lanes = columns n of C
         int acc = 0;
         uint32_t acc_phase = 0;
+        int failed_tile = -1;     // this warp's first slab whose accumulator never arrived
         for (int nt = blockIdx.x; nt < p.num_n_tiles; nt += gridDim.x) {
             int ok = 1;
             if (lane == 0)
-                ok = mbar_wait(accf_bar(acc), acc_phase) ? 1 : 0;
+                ok = mbar_wait(accf_bar(acc), acc_phase, p.wait_limit_ns) ? 1 : 0;
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) {
-                if (lane == 0)
+                if (lane == 0) {
                     report_status(kStatusEpilogueTimeout);
+                    *fail_flag_ptr = 1u;
+                }
+                failed_tile = nt;
                 break;
             }
             tc_fence_after();
@@ -264,6 +272,11 @@ tc_skinny_kernel(const __grid_constant__ CUtensorMap map_bt, const __grid_consta
             }
         }
         __syncwarp();
+        if (failed_tile >= 0 && splits == 1) {
+            // This warp's 32 columns of C (all m rows) in every slab from the failed one on.
+            for (int nt = failed_tile; nt < p.num_n_tiles; nt += gridDim.x)
+                fill_nan(p.c, p.m, p.n, 0, p.m, nt * SK_BM + quarter * 32, 32, 0, 1, lane);
+        }
     }
 
     if (splits > 1 && kPartialBytes + static_cast<uint32_t>(splits - 1) * (kPartialBytes / splits) >
@@ -277,6 +290,9 @@ tc_skinny_kernel(const __grid_constant__ CUtensorMap map_bt, const __grid_consta
         if (threadIdx.x == 0)
             mbar_arrive_expect_tx(recv_bar, static_cast<uint32_t>(splits - 1) * slice_bytes);
         cluster_sync_all();     // every CTA of the cluster is past its main loop: rings idle
+        // A CTA whose progress wait ran out has no valid partial: the columns of
+        // every CTA of the cluster become NaN.
+        const bool any_failed = cluster_any_failed(fail_flag, splits);
         if (warp >= 2) {
             const int quarter = warp & 3;
             const uint32_t row_addr = s_a + static_cast<uint32_t>(quarter * 32 + lane) * kPartialPitch;
@@ -314,9 +330,11 @@ tc_skinny_kernel(const __grid_constant__ CUtensorMap map_bt, const __grid_consta
             received = mbar_wait(recv_bar, 0) ? 1 : 0;
         received = __shfl_sync(0xffffffffu, received, 0);
         if (!received && lane == 0)
-            report_status(kStatusEpilogueTimeout);
+            report_status(kStatusDrainTimeout);
+        if (any_failed || !received)
+            fill_nan(p.c, p.m, p.n, 0, p.m, nt * SK_BM + split * rows, rows, warp, TC_THREADS / 32, lane);
         const uint8_t *ring = smem_raw + (s_a - raw);
-        for (int idx = threadIdx.x; received && idx < p.m * rows; idx += TC_THREADS) {
+        for (int idx = threadIdx.x; received && !any_failed && idx < p.m * rows; idx += TC_THREADS) {
             const int row = idx / rows, rl = idx % rows;    // C row (m), column offset within the slice
             const uint32_t offset = static_cast<uint32_t>(rl) * kPartialPitch + static_cast<uint32_t>(row) * 4;
             float sum = 0.0f;

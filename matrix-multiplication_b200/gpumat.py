@@ -1,178 +1,290 @@
-"""ctypes loader for the B200 GEMM library (``build/b200_matmul.so``).
+"""ctypes binding of the B200 GEMM library (``build/b200_matmul.so``).
 
-Mirror of the reference's ``src/gpumat.py`` (``NativeMatmul``, :15-155) with
-the same constructor, ``configuration()``, ``prepare()``, ``close()`` and
-error behaviour:
+The reference's harness reaches its CUDA library through ``src/gpumat.py``
+(``NativeMatmul``, :15-155).  This module offers the same public surface, so
+that harness code written against it runs unchanged:
 
-* the library path defaults to ``<repo>/build/b200_matmul.so`` and a missing
-  file raises FileNotFoundError (there is no fallback of any kind);
-* the ABI version must be 3 (gpumat.py:31-44);
-* ``prepare`` validates the operands (TypeError / ValueError), captures the
-  current stream, calls ``record_stream`` on every tensor and returns a
-  ``run()`` closure that keeps a, b and out alive and raises RuntimeError
-  on a nonzero native return or after ``close()`` (gpumat.py:119-155).
+    NativeMatmul(library=None, device=0)
+        .configuration(implementation, precision)   -> dict (kernel geometry)
+        .prepare(implementation, a, b, out, *, precision) -> run()
+        .close(), ``with NativeMatmul(...) as native:``
+
+and it fails the same way: FileNotFoundError for a missing library,
+RuntimeError for a wrong ABI version, ValueError / TypeError for bad arguments
+and operand contracts (``precision.validate_operands``), and
+``RuntimeError("<operation> failed: <detail>")`` for a nonzero native return or
+a closed context.
+
+The structure is this library's own:
+
+* ``EXPORTS`` declares every C entry point of ``include/b200_matmul.h`` once,
+  with its argument and result types; ``Library`` loads one copy of the .so per
+  path, checks the ABI version and binds the whole table.
+* Every export except ``matmul_abi_version`` and ``matmul_create`` returns 0/1
+  and takes a caller-owned error buffer as its last two arguments;
+  ``Library.invoke`` supplies the buffer and turns a nonzero return into the
+  RuntimeError above.
+* ``NativeMatmul`` owns one device context.  ``prepare`` returns a
+  ``PreparedLaunch``: the launch's arguments marshalled once (pointers, sizes,
+  the current stream, an error buffer), plus references to the tensors and the
+  stream, so that a call costs one ctypes call and the operands stay alive as
+  long as the launch does.
 
 Implementation names map to this library's ids: ``tcgen05`` -> 7, ``ffma`` -> 8.
+There is no fallback of any kind: without the library nothing runs.
 """
 
 from __future__ import annotations
 
 import ctypes
 import json
+import threading
 from pathlib import Path
 
 import torch
 
-from precision import PRECISION_IDS, unsupported_reason, validate_operands
+from precision import INPUT_DTYPES, PRECISION_IDS, unsupported_reason, validate_operands
 
-_IMPLEMENTATIONS = {"tcgen05": 7, "ffma": 8}
-_ERROR_SIZE = 1024
-_INT_MAX = 2**31 - 1
+ABI_VERSION = 3
+IMPLEMENTATION_IDS = {"tcgen05": 7, "ffma": 8}
 DEFAULT_LIBRARY = Path(__file__).resolve().parent.parent / "build" / "b200_matmul.so"
+ERROR_BYTES = 1024
+JSON_BYTES = 1024
+_INT_MAX = 2**31 - 1
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_ERROR_ARGS = (ctypes.c_char_p, ctypes.c_size_t)
+_MATRIX_CALL = (_P, _I, _I, _P, _P, _P, _I, _I, _I, _P)
+
+# name -> (argument types without the trailing error buffer, result type, takes an error buffer)
+EXPORTS: dict[str, tuple[tuple, object, bool]] = {
+    "matmul_abi_version": ((), ctypes.c_int, False),
+    "matmul_kernel_info": ((_I, _I, ctypes.c_char_p, ctypes.c_size_t), ctypes.c_int, True),
+    "matmul_create": ((_I,), _P, True),
+    "matmul_destroy": ((_P,), ctypes.c_int, True),
+    "matmul_launch": (_MATRIX_CALL, ctypes.c_int, True),
+    "matmul_launch_noalloc": (_MATRIX_CALL, ctypes.c_int, True),
+    "matmul_convert": ((_P, _I, _P, _P, ctypes.c_size_t, _P), ctypes.c_int, True),
+    "matmul_device_status": ((_P, _I, ctypes.POINTER(ctypes.c_uint)), ctypes.c_int, True),
+    "matmul_check_fp64": ((_P, _I, _P, _P, _P, _I, _I, _I, _P, ctypes.POINTER(ctypes.c_double)), ctypes.c_int,
+                          True),
+    "matmul_plan": ((_P, _I, _I, _I, _I, _I, ctypes.c_char_p, ctypes.c_size_t), ctypes.c_int, True),
+    "matmul_set_sm_limit": ((_P, _I), ctypes.c_int, True),
+    "matmul_set_wait_limit": ((_P, ctypes.c_ulonglong), ctypes.c_int, True),
+}
+
+
+def _library_path(library: str | Path | None) -> Path:
+    path = Path(library) if library is not None else DEFAULT_LIBRARY
+    if not path.is_file():
+        raise FileNotFoundError(
+            f"Native matmul library not found at {path}. Build it with "
+            "`python matrix-multiplication_b200/build.py` or pass a library path.")
+    return path.resolve()
+
+
+class Library:
+    """One loaded copy of the library with every export of ``EXPORTS`` bound."""
+
+    _open: dict[Path, "Library"] = {}
+    _lock = threading.Lock()
+
+    def __init__(self, path: Path):
+        try:
+            self.cdll = ctypes.CDLL(str(path))
+        except OSError as exc:
+            raise OSError(f"Could not load native matmul library at {path}: {exc}") from exc
+        self.path = path
+        missing = [name for name in EXPORTS if not hasattr(self.cdll, name)]
+        if "matmul_abi_version" in missing:
+            raise RuntimeError(f"Native matmul library at {path} has no ABI version; rebuild it.")
+        self.cdll.matmul_abi_version.argtypes = []
+        self.cdll.matmul_abi_version.restype = ctypes.c_int
+        version = self.cdll.matmul_abi_version()
+        if version != ABI_VERSION:
+            raise RuntimeError(f"Native matmul library at {path} has ABI version {version}, expected "
+                               f"{ABI_VERSION}; rebuild it.")
+        if missing:
+            raise RuntimeError(f"Native matmul library at {path} lacks {', '.join(missing)}; rebuild it.")
+        for name, (argtypes, restype, with_error) in EXPORTS.items():
+            function = getattr(self.cdll, name)
+            function.argtypes = list(argtypes) + (list(_ERROR_ARGS) if with_error else [])
+            function.restype = restype
+
+    @classmethod
+    def open(cls, library: str | Path | None = None) -> "Library":
+        path = _library_path(library)
+        with cls._lock:
+            if path not in cls._open:
+                cls._open[path] = cls(path)
+            return cls._open[path]
+
+    @staticmethod
+    def failure(operation: str, error) -> RuntimeError:
+        detail = error.value.decode("utf-8", errors="replace")
+        return RuntimeError(f"{operation} failed: {detail or 'unknown native error'}")
+
+    def invoke(self, name: str, *args):
+        """Call export ``name`` with a fresh error buffer; RuntimeError on a nonzero return."""
+        error = ctypes.create_string_buffer(ERROR_BYTES)
+        result = getattr(self.cdll, name)(*args, error, len(error))
+        if name == "matmul_create":
+            if not result:
+                raise self.failure(name, error)
+        elif result != 0:
+            raise self.failure(name, error)
+        return result
+
+    def kernel_info(self, implementation: str, precision: str) -> dict:
+        """``matmul_kernel_info`` as a dict (needs no GPU)."""
+        text = ctypes.create_string_buffer(JSON_BYTES)
+        self.invoke("matmul_kernel_info", IMPLEMENTATION_IDS[implementation], PRECISION_IDS[precision], text,
+                    len(text))
+        return json.loads(text.value)
+
+
+class PreparedLaunch:
+    """One GEMM launch with its arguments marshalled once (``NativeMatmul.prepare``).
+
+    Calling it enqueues ``matmul_launch`` on the stream that was current at
+    ``prepare`` time and returns ``out``.  It holds a, b, out and the stream, so
+    none of them can be freed while the launch object exists.
+    """
+
+    __slots__ = ("_owner", "_function", "_arguments", "_error", "_tensors", "_stream", "out")
+
+    def __init__(self, owner: "NativeMatmul", implementation: int, precision: int, a, b, out, m, k, n, stream):
+        self._owner = owner
+        self._function = owner.library.matmul_launch
+        self._error = ctypes.create_string_buffer(ERROR_BYTES)
+        self._arguments = (implementation, precision, _P(a.data_ptr()), _P(b.data_ptr()), _P(out.data_ptr()),
+                           m, k, n, _P(stream.cuda_stream), self._error, len(self._error))
+        self._tensors = (a, b, out)
+        self._stream = stream
+        self.out = out
+
+    def __call__(self):
+        handle = self._owner._handle
+        if handle is None:
+            raise RuntimeError("NativeMatmul context is closed")
+        if self._function(handle, *self._arguments) != 0:
+            raise Library.failure("matmul_launch", self._error)
+        return self.out
 
 
 class NativeMatmul:
-    """Own a native B200 matmul context for one CUDA device."""
+    """A context of the native B200 GEMM library on one CUDA device."""
 
     def __init__(self, library: str | Path | None = None, device: int = 0):
         if isinstance(device, bool) or not isinstance(device, int) or not 0 <= device <= _INT_MAX:
             raise ValueError("device must be a non-negative CUDA device index")
-        path = Path(library) if library is not None else DEFAULT_LIBRARY
-        if not path.is_file():
-            raise FileNotFoundError(
-                f"Native matmul library not found at {path}. Run "
-                "`python matrix-multiplication_b200/build.py` or pass a library path."
-            )
-        try:
-            self._library = ctypes.CDLL(str(path.resolve()))
-        except OSError as exc:
-            raise OSError(f"Could not load native matmul library at {path}: {exc}") from exc
-        try:
-            abi_version = self._library.matmul_abi_version
-        except AttributeError as exc:
-            raise RuntimeError(f"Native matmul library at {path} has no ABI version; rebuild it.") from exc
-        abi_version.argtypes = []
-        abi_version.restype = ctypes.c_int
-        version = abi_version()
-        if version != 3:
-            raise RuntimeError(f"Native matmul library at {path} has ABI version {version}, expected 3; rebuild it.")
-        self.path = path.resolve()
-        _bind(self._library)
+        self._handle = None
+        self._lib = Library.open(library)
+        self.path = self._lib.path
         self._device = device
-        self._context = None
-        error = ctypes.create_string_buffer(_ERROR_SIZE)
-        context = self._library.matmul_create(device, error, len(error))
-        if not context:
-            raise RuntimeError(self._error_message("matmul_create", error))
-        self._context = context
+        self._handle = _P(self._lib.invoke("matmul_create", device))
         self._capability = torch.cuda.get_device_capability(device)
 
-    @staticmethod
-    def _error_message(operation, error):
-        detail = error.value.decode("utf-8", errors="replace")
-        return f"{operation} failed: {detail or 'unknown native error'}"
-
+    # ---------------------------------------------------------------- lifetime
     @property
     def device(self) -> int:
         return self._device
 
-    def close(self):
-        """Destroy the context once; prepared operations cannot be used afterward."""
-        context = self._context
-        if context is not None:
-            self._context = None
-            error = ctypes.create_string_buffer(_ERROR_SIZE)
-            if self._library.matmul_destroy(context, error, len(error)) != 0:
-                raise RuntimeError(self._error_message("matmul_destroy", error))
+    @property
+    def library(self):
+        """The bound ctypes library (every export of ``EXPORTS``)."""
+        return self._lib.cdll
+
+    @property
+    def handle(self):
+        """The native context pointer; RuntimeError once the context is closed."""
+        if self._handle is None:
+            raise RuntimeError("NativeMatmul context is closed")
+        return self._handle
+
+    @property
+    def closed(self) -> bool:
+        return self._handle is None
+
+    def close(self) -> None:
+        """Destroy the context (once); prepared launches fail afterwards."""
+        handle, self._handle = self._handle, None
+        if handle is not None:
+            self._lib.invoke("matmul_destroy", handle)
 
     def __enter__(self):
-        if self._context is None:
-            raise RuntimeError("NativeMatmul context is closed")
+        self.handle
         return self
 
-    def __exit__(self, exc_type, exc_value, traceback):
+    def __exit__(self, *exc_info):
         self.close()
 
     def __del__(self):
         try:
-            if getattr(self, "_context", None) is not None:
-                self.close()
+            self.close()
         except Exception:
             pass
 
-    def configuration(self, implementation: str, precision: str = "fp32") -> dict:
-        """Return the native kernel's launch geometry and staging policy."""
-        if self._context is None:
-            raise RuntimeError("NativeMatmul context is closed")
-        if not isinstance(implementation, str) or implementation not in _IMPLEMENTATIONS:
+    # ---------------------------------------------------------------- argument checks
+    def _implementation_id(self, implementation) -> int:
+        if not isinstance(implementation, str) or implementation not in IMPLEMENTATION_IDS:
             raise ValueError(f"unknown implementation: {implementation!r}")
+        return IMPLEMENTATION_IDS[implementation]
+
+    def _require_supported(self, implementation: str, precision: str) -> None:
+        reason = unsupported_reason(implementation, precision, self._capability)
+        if reason is not None:
+            raise ValueError(reason)
+
+    # ---------------------------------------------------------------- the reference's surface
+    def configuration(self, implementation: str, precision: str = "fp32") -> dict:
+        """The kernel's geometry and staging policy (``matmul_kernel_info``)."""
+        self.handle
+        self._implementation_id(implementation)
         if not isinstance(precision, str) or precision not in PRECISION_IDS:
             raise ValueError(f"unknown precision: {precision!r}")
-        reason = unsupported_reason(implementation, precision, self._capability)
-        if reason is not None:
-            raise ValueError(reason)
-        return kernel_info(self._library, implementation, precision)
+        self._require_supported(implementation, precision)
+        return self._lib.kernel_info(implementation, precision)
 
-    def prepare(self, implementation: str, a: torch.Tensor, b: torch.Tensor, out: torch.Tensor,
-                *, precision: str = "fp32"):
-        """Prepare an asynchronous operation on the current CUDA stream."""
-        if self._context is None:
-            raise RuntimeError("NativeMatmul context is closed")
-        if not isinstance(implementation, str) or implementation not in _IMPLEMENTATIONS:
-            raise ValueError(f"unknown implementation: {implementation!r}")
+    def prepare(self, implementation: str, a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, *,
+                precision: str = "fp32") -> PreparedLaunch:
+        """Validate the operands once and return a launch on the current CUDA stream."""
+        self.handle
+        implementation_id = self._implementation_id(implementation)
         m, k, n = validate_operands(a, b, out, precision, self._device)
-        reason = unsupported_reason(implementation, precision, self._capability)
-        if reason is not None:
-            raise ValueError(reason)
-        a_ptr = ctypes.c_void_p(a.data_ptr())
-        b_ptr = ctypes.c_void_p(b.data_ptr())
-        out_ptr = ctypes.c_void_p(out.data_ptr())
+        self._require_supported(implementation, precision)
         stream = torch.cuda.current_stream(self._device)
-        stream_ptr = ctypes.c_void_p(stream.cuda_stream)
         for tensor in (a, b, out):
             tensor.record_stream(stream)
-        implementation_id = _IMPLEMENTATIONS[implementation]
-        precision_id = PRECISION_IDS[precision]
-        launch = self._library.matmul_launch
-        error = ctypes.create_string_buffer(_ERROR_SIZE)
+        return PreparedLaunch(self, implementation_id, PRECISION_IDS[precision], a, b, out, m, k, n, stream)
 
-        def run():
-            _ = a, b, stream
-            context = self._context
-            if context is None:
-                raise RuntimeError("NativeMatmul context is closed")
-            if launch(context, implementation_id, precision_id, a_ptr, b_ptr, out_ptr, m, k, n,
-                      stream_ptr, error, len(error)) != 0:
-                raise RuntimeError(self._error_message("matmul_launch", error))
-            return out
-
-        return run
-
+    # ---------------------------------------------------------------- this library's additions
     def plan(self, implementation: str, m: int, k: int, n: int, precision: str = "fp32") -> dict:
         """The launch ``prepare(...)()`` would make for an m x k x n problem (kernel,
         tile, K splits; the FFMA plan assumes 16-byte aligned operands)."""
-        if self._context is None:
-            raise RuntimeError("NativeMatmul context is closed")
-        if not isinstance(implementation, str) or implementation not in _IMPLEMENTATIONS:
-            raise ValueError(f"unknown implementation: {implementation!r}")
+        handle = self.handle
+        implementation_id = self._implementation_id(implementation)
         if not isinstance(precision, str) or precision not in PRECISION_IDS:
             raise ValueError(f"unknown precision: {precision!r}")
-        result = ctypes.create_string_buffer(_ERROR_SIZE)
-        error = ctypes.create_string_buffer(_ERROR_SIZE)
-        if self._library.matmul_plan(self._context, _IMPLEMENTATIONS[implementation], PRECISION_IDS[precision],
-                                     m, k, n, result, len(result), error, len(error)) != 0:
-            raise RuntimeError(self._error_message("matmul_plan", error))
-        return json.loads(result.value)
+        text = ctypes.create_string_buffer(JSON_BYTES)
+        self._lib.invoke("matmul_plan", handle, implementation_id, PRECISION_IDS[precision], m, k, n, text,
+                         len(text))
+        return json.loads(text.value)
 
     def set_sm_limit(self, sms: int) -> None:
         """Run later tensor-core launches on at most ``sms`` SMs (0 = all of them)."""
-        if self._context is None:
-            raise RuntimeError("NativeMatmul context is closed")
+        handle = self.handle
         if isinstance(sms, bool) or not isinstance(sms, int):
             raise TypeError("sms must be an int")
-        error = ctypes.create_string_buffer(_ERROR_SIZE)
-        if self._library.matmul_set_sm_limit(self._context, sms, error, len(error)) != 0:
-            raise RuntimeError(self._error_message("matmul_set_sm_limit", error))
+        self._lib.invoke("matmul_set_sm_limit", handle, sms)
+
+    def set_wait_limit(self, nanoseconds: int) -> None:
+        """Limit the tensor-core kernels' progress waits (0 = the default 2 s)."""
+        handle = self.handle
+        if isinstance(nanoseconds, bool) or not isinstance(nanoseconds, int) or nanoseconds < 0:
+            raise ValueError("the wait limit is a non-negative number of nanoseconds")
+        self._lib.invoke("matmul_set_wait_limit", handle, nanoseconds)
 
     def convert(self, src: torch.Tensor, dst: torch.Tensor, precision: str) -> torch.Tensor:
         """Convert FP32 ``src`` into ``dst`` (the input dtype of ``precision``) on the device.
@@ -180,12 +292,9 @@ class NativeMatmul:
         BF16/FP16 round to nearest even; TF32 keeps FP32 storage rounded to 10
         fraction bits (ties to even); FP32 copies.
         """
-        if self._context is None:
-            raise RuntimeError("NativeMatmul context is closed")
+        handle = self.handle
         if precision not in PRECISION_IDS:
             raise ValueError(f"Unknown precision: {precision}")
-        from precision import INPUT_DTYPES
-
         if src.dtype != torch.float32 or dst.dtype != getattr(torch, INPUT_DTYPES[precision]):
             raise TypeError("src must be float32 and dst the input dtype of the precision")
         for tensor in (src, dst):
@@ -194,11 +303,8 @@ class NativeMatmul:
         if src.numel() != dst.numel():
             raise ValueError("src and dst must have the same number of elements")
         stream = torch.cuda.current_stream(self._device)
-        error = ctypes.create_string_buffer(_ERROR_SIZE)
-        if self._library.matmul_convert(self._context, PRECISION_IDS[precision], ctypes.c_void_p(src.data_ptr()),
-                                        ctypes.c_void_p(dst.data_ptr()), src.numel(),
-                                        ctypes.c_void_p(stream.cuda_stream), error, len(error)) != 0:
-            raise RuntimeError(self._error_message("matmul_convert", error))
+        self._lib.invoke("matmul_convert", handle, PRECISION_IDS[precision], _P(src.data_ptr()),
+                         _P(dst.data_ptr()), src.numel(), _P(stream.cuda_stream))
         return dst
 
     def check_fp64(self, a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, precision: str) -> tuple[float, float]:
@@ -207,84 +313,32 @@ class NativeMatmul:
         Returns (largest tolerance ratio, largest absolute error); a ratio <= 1
         passes the reference's roundoff-aware allowance.  Synchronizes.
         """
-        if self._context is None:
-            raise RuntimeError("NativeMatmul context is closed")
+        handle = self.handle
         m, k, n = validate_operands(a, b, out, precision, self._device)
         stream = torch.cuda.current_stream(self._device)
         result = (ctypes.c_double * 2)()
-        error = ctypes.create_string_buffer(_ERROR_SIZE)
-        if self._library.matmul_check_fp64(self._context, PRECISION_IDS[precision], ctypes.c_void_p(a.data_ptr()),
-                                           ctypes.c_void_p(b.data_ptr()), ctypes.c_void_p(out.data_ptr()), m, k, n,
-                                           ctypes.c_void_p(stream.cuda_stream), result, error, len(error)) != 0:
-            raise RuntimeError(self._error_message("matmul_check_fp64", error))
+        self._lib.invoke("matmul_check_fp64", handle, PRECISION_IDS[precision], _P(a.data_ptr()),
+                         _P(b.data_ptr()), _P(out.data_ptr()), m, k, n, _P(stream.cuda_stream), result)
         return float(result[0]), float(result[1])
 
     def device_status(self, clear: bool = True) -> int:
-        """Synchronize and return the device status word (0 = no kernel timed out)."""
-        if self._context is None:
-            raise RuntimeError("NativeMatmul context is closed")
+        """Synchronize and return the device status word (0 = no kernel's wait ran out)."""
+        handle = self.handle
         status = ctypes.c_uint(0)
-        error = ctypes.create_string_buffer(_ERROR_SIZE)
-        if self._library.matmul_device_status(self._context, int(bool(clear)), ctypes.byref(status),
-                                              error, len(error)) != 0:
-            raise RuntimeError(self._error_message("matmul_device_status", error))
+        self._lib.invoke("matmul_device_status", handle, int(bool(clear)), ctypes.byref(status))
         return int(status.value)
 
 
-def _bind(library) -> None:
-    library.matmul_create.argtypes = [ctypes.c_int, ctypes.c_char_p, ctypes.c_size_t]
-    library.matmul_create.restype = ctypes.c_void_p
-    library.matmul_destroy.argtypes = [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_size_t]
-    library.matmul_destroy.restype = ctypes.c_int
-    library.matmul_launch.argtypes = [
-        ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
-        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
-        ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
-        ctypes.c_char_p, ctypes.c_size_t,
-    ]
-    library.matmul_launch.restype = ctypes.c_int
-    library.matmul_kernel_info.argtypes = [
-        ctypes.c_int, ctypes.c_int, ctypes.c_char_p, ctypes.c_size_t, ctypes.c_char_p, ctypes.c_size_t,
-    ]
-    library.matmul_kernel_info.restype = ctypes.c_int
-    library.matmul_convert.argtypes = [
-        ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
-        ctypes.c_char_p, ctypes.c_size_t,
-    ]
-    library.matmul_convert.restype = ctypes.c_int
-    library.matmul_device_status.argtypes = [
-        ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_uint), ctypes.c_char_p, ctypes.c_size_t,
-    ]
-    library.matmul_device_status.restype = ctypes.c_int
-    library.matmul_check_fp64.argtypes = [
-        ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
-        ctypes.c_int, ctypes.c_void_p, ctypes.POINTER(ctypes.c_double), ctypes.c_char_p, ctypes.c_size_t,
-    ]
-    library.matmul_check_fp64.restype = ctypes.c_int
-    library.matmul_plan.argtypes = [
-        ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
-        ctypes.c_char_p, ctypes.c_size_t, ctypes.c_char_p, ctypes.c_size_t,
-    ]
-    library.matmul_plan.restype = ctypes.c_int
-    library.matmul_set_sm_limit.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_char_p, ctypes.c_size_t]
-    library.matmul_set_sm_limit.restype = ctypes.c_int
-
-
 def kernel_info(library, implementation: str, precision: str) -> dict:
-    """``matmul_kernel_info`` as a dict (needs no GPU)."""
-    result = ctypes.create_string_buffer(_ERROR_SIZE)
-    error = ctypes.create_string_buffer(_ERROR_SIZE)
-    if library.matmul_kernel_info(_IMPLEMENTATIONS[implementation], PRECISION_IDS[precision], result, len(result),
+    """``matmul_kernel_info`` of a library loaded with ``load_library`` (needs no GPU)."""
+    text = ctypes.create_string_buffer(JSON_BYTES)
+    error = ctypes.create_string_buffer(ERROR_BYTES)
+    if library.matmul_kernel_info(IMPLEMENTATION_IDS[implementation], PRECISION_IDS[precision], text, len(text),
                                   error, len(error)) != 0:
-        raise RuntimeError(NativeMatmul._error_message("matmul_kernel_info", error))
-    return json.loads(result.value)
+        raise Library.failure("matmul_kernel_info", error)
+    return json.loads(text.value)
 
 
 def load_library(library: str | Path | None = None):
-    """Load and bind the library without creating a device context."""
-    path = Path(library) if library is not None else DEFAULT_LIBRARY
-    if not path.is_file():
-        raise FileNotFoundError(f"Native matmul library not found at {path}")
-    handle = ctypes.CDLL(str(path.resolve()))
-    _bind(handle)
-    return handle
+    """The bound ctypes library, without creating a device context."""
+    return Library.open(library).cdll

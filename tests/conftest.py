@@ -82,6 +82,6 @@ def native(gpu_ready, library_path):
 
     context = NativeMatmul(library_path)
     yield context
-    status = context.device_status() if context._context is not None else 0
+    status = context.device_status() if not context.closed else 0
     context.close()
     assert status == 0, f"a kernel reported a bounded-wait timeout (status {status:#x})"

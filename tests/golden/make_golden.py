@@ -1,9 +1,8 @@
 """Generate the golden vectors that pin the CPU oracle to the reference.
 
-Run in a checkout that has the reference next to it (the default path is the
-read-only reference mount of the development container)::
+Run where a checkout of the reference is available::
 
-    python tests/golden/make_golden.py [--reference /path/to/matrix-multiplication]
+    python tests/golden/make_golden.py --reference /path/to/matrix-multiplication
 
 It imports the reference's own ``src/precision.py`` (quantize_inputs,
 reference_product, GemmReference) and writes ``precision_golden.npz`` beside
@@ -59,7 +58,8 @@ def quantize_probe() -> np.ndarray:
 
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__)
-    parser.add_argument("--reference", type=Path, default=Path("/root/reference"))
+    parser.add_argument("--reference", type=Path, required=True,
+                        help="checkout of chudinovAI/matrix-multiplication (its src/precision.py is imported)")
     args = parser.parse_args()
     ref = load_reference(args.reference)
     out = {}

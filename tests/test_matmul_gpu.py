@@ -411,7 +411,7 @@ def test_precision_contracts(native):
 
 def test_native_launch_rejects_bad_arguments(native):
     """The C entry point itself rejects bad ids and sizes (matmul.cu:354-367)."""
-    lib = native._library
+    lib = native.library
     a = torch.ones((2, 2), device="cuda")
     out = torch.empty((2, 2), device="cuda")
     err = ctypes.create_string_buffer(256)
@@ -420,11 +420,11 @@ def test_native_launch_rejects_bad_arguments(native):
     o = ctypes.c_void_p(out.data_ptr())
     for impl, prec, m, k, n in ((7, 0, 2, 2, 2), (8, 3, 2, 2, 2), (6, 3, 2, 2, 2), (8, 0, 0, 2, 2),
                                 (8, 0, 2, -1, 2), (99, 0, 2, 2, 2)):
-        assert lib.matmul_launch(native._context, impl, prec, p, p, o, m, k, n, stream, err, len(err)) == 1
+        assert lib.matmul_launch(native.handle, impl, prec, p, p, o, m, k, n, stream, err, len(err)) == 1
         assert err.value.decode().startswith("matmul_launch: ")
     odd = ctypes.c_void_p(a.data_ptr() + 1)
-    assert lib.matmul_launch(native._context, 8, 0, odd, p, o, 1, 1, 1, stream, err, len(err)) == 1
-    assert lib.matmul_launch(native._context, 8, 0, None, p, o, 1, 1, 1, stream, err, len(err)) == 1
+    assert lib.matmul_launch(native.handle, 8, 0, odd, p, o, 1, 1, 1, stream, err, len(err)) == 1
+    assert lib.matmul_launch(native.handle, 8, 0, None, p, o, 1, 1, 1, stream, err, len(err)) == 1
 
 
 def test_partial_overlap_rejected_but_disjoint_storage_works(native):

@@ -7,8 +7,10 @@ entry point whose scratch (TF32-rounded and repacked operand copies) lives in
 a fixed 32 MiB array compiled into the library.  These tests call it through
 the C-ABI and check that, on two calls in a row, it gives the same output as
 matmul_launch (within the tolerance used by every other parity test here, and
-against the FP64 oracle), and that a problem too large for the array is
-rejected with a clear error.  The file name makes pytest collect it last.
+against the FP64 oracle) on every kind of scratch use: TF32 rounding copies for
+the single-CTA and skinny kernels, and repacked unaligned FP16/BF16 operands,
+split K included; and that a problem too large for the array is rejected with a
+clear error.  The file name makes pytest collect it last.
 """
 
 from __future__ import annotations
@@ -55,21 +57,29 @@ def _launch(fn, native, precision, a, b, out):
     m, k = a.shape
     n = b.shape[1]
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-    rc = fn(native._context, TCGEN05, PRECISION_IDS[precision], ctypes.c_void_p(a.data_ptr()),
+    rc = fn(native.handle, TCGEN05, PRECISION_IDS[precision], ctypes.c_void_p(a.data_ptr()),
             ctypes.c_void_p(b.data_ptr()), ctypes.c_void_p(out.data_ptr()), m, k, n, stream, err, len(err))
     return rc, err.value.decode()
 
 
+# TF32 problems above m*k*n = 2^25 run on the tensor cores and place their rounded
+# copies of A and B^T in the fixed array; smaller ones run on the FFMA kernel and
+# need no scratch, so every TF32 case here is above that size.
 @pytest.mark.parametrize("precision,shape,offset", [
-    ("tf32", (300, 200, 500), False),     # scratch: rounded A and transposed B
-    ("tf32", (129, 65, 257), True),       # scratch, unaligned operands
+    ("tf32", (384, 260, 516), False),     # scratch: rounded A and transposed B (single-CTA tiles)
+    ("tf32", (257, 300, 515), True),      # scratch: the same from unaligned operands
+    ("tf32", (512, 1024, 512), False),    # scratch: 4 MiB of rounded copies
+    ("tf32", (48, 1024, 1024), False),    # scratch: rounded copies feeding the skinny (m <= 64) kernel
     ("bf16", (513, 129, 577), True),      # scratch: repacked unaligned operands
+    ("bf16", (130, 4099, 258), True),     # scratch: repacked operands of a split-K launch
     ("fp16", (256, 512, 512), False),     # aligned: no scratch needed
 ])
 def test_noalloc_matches_matmul_launch_on_two_calls(native, precision, shape, offset):
-    lib = native._library
+    lib = native.library
     _bind(lib)
     m, k, n = shape
+    plan = native.plan("tcgen05", m, k, n, precision=precision)
+    assert plan["kernel"] in ("tc_single", "tc2_pair", "tc_skinny"), plan
     a_np, b_np, a, b = _operands(precision, m, k, n, offset)
     expected = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
     rc, msg = _launch(lib.matmul_launch, native, precision, a, b, expected)
@@ -86,7 +96,7 @@ def test_noalloc_matches_matmul_launch_on_two_calls(native, precision, shape, of
 
 
 def test_noalloc_rejects_problems_beyond_the_fixed_array(native):
-    lib = native._library
+    lib = native.library
     _bind(lib)
     m = k = n = 4096                      # TF32 copies need 128 MiB > 32 MiB
     a = torch.zeros((m, k), dtype=torch.float32, device="cuda")
@@ -99,13 +109,13 @@ def test_noalloc_rejects_problems_beyond_the_fixed_array(native):
 
 
 def test_noalloc_accepts_only_the_tcgen05_implementation(native):
-    lib = native._library
+    lib = native.library
     _bind(lib)
     a = torch.ones((2, 2), dtype=torch.float32, device="cuda")
     out = torch.empty((2, 2), dtype=torch.float32, device="cuda")
     err = ctypes.create_string_buffer(256)
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     p = ctypes.c_void_p(a.data_ptr())
-    rc = lib.matmul_launch_noalloc(native._context, 8, 0, p, p, ctypes.c_void_p(out.data_ptr()), 2, 2, 2, stream,
+    rc = lib.matmul_launch_noalloc(native.handle, 8, 0, p, p, ctypes.c_void_p(out.data_ptr()), 2, 2, 2, stream,
                                    err, len(err))
     assert rc == 1 and err.value.decode().startswith("matmul_launch_noalloc: ")
