@@ -413,7 +413,13 @@ def single_gpu(args) -> dict:
     traffic_file = ROOT / "profiles" / "ncu_traffic.json"
     if traffic_file.exists():
         traffic = json.loads(traffic_file.read_text()).get(f"{plan['kernel']}_{plan['tile_m']}x{plan['tile_n']}_bf16_8192")
-    peak = peaks["bf16_tflops"]
+    # The timed region is K replays of 10 GEMMs back to back: when the clock record
+    # shows the power cap, the kernel ran in the sustained regime and the sustained
+    # cuBLAS figure is its denominator; otherwise the burst figure.
+    sustained = "sw_power_cap" in (clock_summary.get("reasons") or []) and "bf16_tflops_sustained" in peaks
+    peak = peaks["bf16_tflops_sustained"] if sustained else peaks["bf16_tflops"]
+    peak_name = "bf16_tflops_sustained (cuBLAS 8192^3 back to back for 4 s)" if sustained else \
+        "bf16_tflops (burst, cuBLAS 8192^3)"
     return {
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
@@ -432,7 +438,8 @@ def single_gpu(args) -> dict:
         "burst": burst,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "traffic": traffic,
-                     "peak_source": f"{peak_kind} bf16_tflops (burst, cuBLAS 8192^3)",
+                     "peak_source": f"{peak_kind} {peak_name}",
+                     "frac_of_burst_peak": achieved / peaks["bf16_tflops"],
                      "kernel": f"{plan['kernel']} {plan['tile_m']}x{plan['tile_n']} BF16", "kernel_ms": kernel_ms,
                      "kernel_ms_source": "median graph step / GEMMs per step (CUDA events on the launching stream)",
                      "algorithmic_flops_per_launch": 2.0 * m * k * n},
@@ -448,43 +455,71 @@ def single_gpu(args) -> dict:
 
 # ---------------------------------------------------------------- multi GPU
 def multi_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
+    """Row-sharded 32768^3 BF16 GEMM over `world` ranks (one process per GPU).
+
+    A step: broadcast of the next step's B (NCCL, own communicator, one step
+    ahead), the local rows' GEMMs in row chunks, and the C all-gather of every
+    chunk as soon as it is done -- by copy-engine pushes into the peers' C
+    (``--exchange ce``, no SM taken from the GEMM) or by grouped NCCL send/recv
+    (``--exchange nccl``).  Time per step = max over ranks of CUDA-event time.
+    The same run also measures, on every rank: the gather-to-rank-0 variant,
+    each part of a step alone (GEMMs, broadcast, exchange), T1 (the whole
+    problem on one GPU, all GPUs at once), an FP64 check of rows received from
+    a peer, and an end-to-end step from pinned FP32 host buffers.
+    """
     import datetime
 
     import torch
     import torch.distributed as dist
 
     from gpumat import NativeMatmul
-    from sharded import BroadcastPipeline, ShardPlan, pipelined_step
+    from sharded import BroadcastPipeline, CopyEngineGather, ShardPlan, pipelined_step, pipelined_step_ce
 
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
-    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=device)
     b_group = dist.new_group(list(range(world)))       # B broadcasts on their own communicator
     size = args.size or 32768
     m = k = n = size
-    plan = ShardPlan(m, k, n, world, rank, chunks=args.chunks, gather=args.gather)
+    plan = ShardPlan(m, k, n, world, rank, chunks=args.chunks, gather="all")
+    plan_root = ShardPlan(m, k, n, world, rank, chunks=args.chunks, gather="root")
     start, stop = plan.local_rows
     native = NativeMatmul(device=local_rank)
     stream = torch.cuda.current_stream(device)
-    gen = torch.Generator(device=device)
-    gen.manual_seed(1000 + rank)
-    a32 = torch.rand((stop - start, k), generator=gen, device=device) * 2 - 1
-    a = torch.empty((stop - start, k), dtype=torch.bfloat16, device=device)
-    native.convert(a32, a, "bf16")
-    del a32
+
+    def shard_a(owner: int) -> torch.Tensor:
+        rows = plan.rows[owner][1] - plan.rows[owner][0]
+        gen = torch.Generator(device=device)
+        gen.manual_seed(1000 + owner)
+        a32 = torch.rand((rows, k), generator=gen, device=device) * 2 - 1
+        out = torch.empty((rows, k), dtype=torch.bfloat16, device=device)
+        native.convert(a32, out, "bf16")
+        return out
+
+    a = shard_a(rank)
     b = torch.empty((k, n), dtype=torch.bfloat16, device=device)
     if rank == 0:
+        gen = torch.Generator(device=device)
         gen.manual_seed(7)
         b32 = torch.rand((k, n), generator=gen, device=device) * 2 - 1
         native.convert(b32, b, "bf16")
         del b32
-    c = torch.empty((m, n), dtype=torch.float32, device=device)
+    use_ce = args.exchange == "ce"
+    if use_ce:
+        import torch.distributed._symmetric_memory as symm_mem
+
+        c = symm_mem.empty((m, n), dtype=torch.float32, device=device)
+        handle = symm_mem.rendezvous(c, dist.group.WORLD)
+        gather_all = CopyEngineGather(plan, c, handle=handle)
+        gather_root = CopyEngineGather(plan_root, c, handle=handle)
+    else:
+        c = torch.empty((m, n), dtype=torch.float32, device=device)
     dist.broadcast(b, src=0)                            # the first step's B, before the loop
     pipe = BroadcastPipeline(b, b_group)
     del b
     sms = torch.cuda.get_device_properties(device).multi_processor_count
-    if args.reserve_sms:
-        native.set_sm_limit(max(2, sms - args.reserve_sms))
+    gemm_sms = max(2, sms - args.reserve_sms) if args.reserve_sms else sms
+    native.set_sm_limit(gemm_sms if gemm_sms < sms else 0)
     runs = {}
 
     def gemm(a_rows, b_full, c_rows):
@@ -493,34 +528,132 @@ def multi_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
             runs[key] = native.prepare("tcgen05", a_rows, b_full, c_rows, precision="bf16")
         runs[key]()
 
-    def step():
-        pipelined_step(plan, a, pipe, c, gemm)
+    def step_all():
+        if use_ce:
+            pipelined_step_ce(plan, a, pipe, gather_all, gemm)
+        else:
+            pipelined_step(plan, a, pipe, c, gemm)
 
-    for _ in range(args.warmup):
-        step()
-    dist.barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local_rank) as clocks:
+    def step_root():
+        if use_ce:
+            pipelined_step_ce(plan_root, a, pipe, gather_root, gemm)
+        else:
+            pipelined_step(plan_root, a, pipe, c, gemm)
+
+    def gemm_only():
+        for lo, hi in plan.chunk_ranges[rank]:
+            gemm(a[lo:hi], pipe.current, c[start + lo:start + hi])
+
+    def broadcast_only():
+        pipe.start()
+        pipe.finish()
+
+    def exchange_only():
+        if use_ce:
+            for index in range(plan.chunk_count):
+                event = torch.cuda.Event()
+                event.record()
+                gather_all.post(index, event)
+            gather_all.finish()
+        else:
+            from sharded import exchange_chunk
+
+            works = []
+            for index in range(plan.chunk_count):
+                works.extend(exchange_chunk(plan, index, c))
+            for work in works:
+                work.wait()
+
+    def timed(fn, steps: int, warmup: int, clocks=None) -> tuple[float, tuple[float, float]]:
+        for _ in range(warmup):
+            fn()
+        dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         wall0 = time.time()
         e0.record(stream)
-        for _ in range(args.steps):
-            step()
+        for _ in range(steps):
+            fn()
         e1.record(stream)
         torch.cuda.synchronize()
         wall1 = time.time()
-    dist.barrier()
-    ms = torch.tensor([e0.elapsed_time(e1) / args.steps], device=device, dtype=torch.float64)
-    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-    ms_per_step = float(ms.item())
+        dist.barrier()
+        ms = torch.tensor([e0.elapsed_time(e1) / steps], device=device, dtype=torch.float64)
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        return float(ms.item()), (wall0, wall1)
+
+    with ClockSampler(local_rank) as clocks:
+        ms_per_step, window = timed(step_all, args.steps, args.warmup)
+    clock_summary = clocks.summary(*window)
+    side_steps = max(3, min(args.steps, 10))
+    breakdown = {
+        "gather_to_rank0_ms": timed(step_root, side_steps, 2)[0],
+        "gemm_only_ms": timed(gemm_only, side_steps, 2)[0],
+        "broadcast_only_ms": timed(broadcast_only, side_steps, 2)[0],
+        "exchange_only_ms": timed(exchange_only, side_steps, 2)[0],
+    }
+
+    # FP64 check of rows this rank received from the next rank (its A shard is
+    # regenerated here from the same seed): the GEMM and the exchange together.
+    timed(step_all, 1, 0)
+    owner = (rank + 1) % world
+    owner_lo = plan.rows[owner][0]
+    band = min(64, plan.rows[owner][1] - owner_lo)
+    a_owner = shard_a(owner)
+    ratio, max_err = native.check_fp64(a_owner[:band], pipe.current, c[owner_lo:owner_lo + band], "bf16")
+    del a_owner
+    check = torch.tensor([ratio, max_err], device=device, dtype=torch.float64)
+    dist.all_reduce(check, op=dist.ReduceOp.MAX)
+
+    # T1: the whole problem on one GPU, measured on every GPU at once (no SM limit).
+    native.set_sm_limit(0)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(2000)
+    a_full32 = torch.rand((m, k), generator=gen, device=device) * 2 - 1
+    a_full = torch.empty((m, k), dtype=torch.bfloat16, device=device)
+    native.convert(a_full32, a_full, "bf16")
+    del a_full32
+    run_full = native.prepare("tcgen05", a_full, pipe.current, c, precision="bf16")
+    t1_ms, _ = timed(run_full, 3, 1)
+    t1_min = torch.tensor([t1_ms], device=device, dtype=torch.float64)
+    del run_full, a_full
+    native.set_sm_limit(gemm_sms if gemm_sms < sms else 0)
+
+    # End to end: pinned FP32 host A shard (every rank) and B (rank 0) -> device,
+    # RNE conversion, the sharded step, this rank's C rows back to pinned host memory.
+    host_a = (torch.rand((stop - start, k), device=device) * 2 - 1).cpu().pin_memory()
+    host_b = (torch.rand((k, n), device=device) * 2 - 1).cpu().pin_memory() if rank == 0 else None
+    host_c = torch.empty((stop - start, n), dtype=torch.float32).pin_memory()
+    dev_a32 = torch.empty((stop - start, k), dtype=torch.float32, device=device)
+    dev_b32 = torch.empty((k, n), dtype=torch.float32, device=device) if rank == 0 else None
+
+    def e2e_step():
+        dev_a32.copy_(host_a, non_blocking=True)
+        native.convert(dev_a32, a, "bf16")
+        if rank == 0:
+            dev_b32.copy_(host_b, non_blocking=True)
+            native.convert(dev_b32, pipe.pending, "bf16")
+        step_all()
+        host_c.copy_(c[start:stop], non_blocking=True)
+
+    e2e_ms, _ = timed(e2e_step, 3, 1)
+    h2d = (stop - start) * k * 4 + (k * n * 4 if rank == 0 else 0)
+    d2h = (stop - start) * n * 4
+    del host_a, host_b, host_c, dev_a32, dev_b32
+
     status = native.device_status()
-    clock_summary = clocks.summary(wall0, wall1)
+    status_t = torch.tensor([status], device=device, dtype=torch.int64)
+    dist.all_reduce(status_t, op=dist.ReduceOp.MAX)
+    dist.all_reduce(t1_min, op=dist.ReduceOp.MIN)
     native.close()
+    if use_ce:
+        del gather_all, gather_root, handle
     dist.barrier()
     dist.destroy_process_group()
     if rank != 0:
         return None
     value = tflops(m, k, n, ms_per_step)
+    t1_value = tflops(m, k, n, t1_ms)
     return {
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
@@ -528,12 +661,28 @@ def multi_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
         "config": {"workload": f"rowshard_bf16_{m}x{k}x{n}", "m": m, "k": k, "n": n, "precision": "bf16",
                    "parallelism": f"row-sharded A/C over {world} ranks; every step broadcasts one B (NCCL, own "
                                   f"communicator, posted one step ahead and overlapping the GEMMs) and "
-                                  f"{'all-gathers' if args.gather == 'all' else 'gathers to rank 0'} C in row "
-                                  f"chunks overlapping the next chunk's GEMM",
-                   "chunks": plan.chunk_count, "gemm_sms": sms - args.reserve_sms if args.reserve_sms else sms,
-                   "l2": "inputs larger than L2"},
+                                  f"all-gathers C in {plan.chunk_count} row chunks, each chunk's exchange "
+                                  f"overlapping the next chunk's GEMM",
+                   "exchange": ("copy-engine pushes into the peers' C (symmetric memory, one cudaMemcpyAsync "
+                                "per peer and chunk), completed by a one-element NCCL all-reduce")
+                   if use_ce else "grouped NCCL send/recv of each chunk",
+                   "chunks": plan.chunk_count, "gemm_sms": gemm_sms, "l2": "inputs larger than L2"},
+        "t1": {"ms": t1_ms, "tflops": t1_value, "fastest_gpu_ms": float(t1_min.item()),
+               "how": "the whole problem as one GEMM on each GPU at once, in the same run (max over GPUs)",
+               "efficiency_vs_t1": t1_ms / (world * ms_per_step)},
+        "breakdown_ms": breakdown,
+        "bound": {"ingress_bytes_per_step_rank1": 2 * k * n + 4 * (m - (plan.rows[1][1] - plan.rows[1][0])) * n,
+                  "ingress_bytes_per_step_rank0": 4 * (m - (stop - start)) * n,
+                  "note": "every rank but 0 must receive one B (BF16) and the other ranks' C rows (FP32) per "
+                          "step; rank 0 only the C rows"},
+        "e2e": {"value": tflops(m, k, n, e2e_ms), "unit": "TFLOP/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "path": "pinned FP32 host A shard (every rank) and B (rank 0) -> H2D -> matmul_convert (RNE) -> "
+                        "sharded step -> D2H of this rank's C rows; rank 0's numbers (max over ranks of time)"},
+        "check": {"check_fp64_ratio_max": float(check[0].item()), "check_fp64_max_abs_err": float(check[1].item()),
+                  "what": "64 rows of the next rank's shard as received by each rank, against an FP64 product"},
         "gpu_launches": args.steps * plan.chunk_count,
-        "clocks": clock_summary, "device_status": status,
+        "clocks": clock_summary, "device_status": int(status_t.item()),
     }
 
 
@@ -549,7 +698,8 @@ def main() -> int:
     parser.add_argument("--chunks", type=int, default=8)
     parser.add_argument("--reserve-sms", type=int, default=16,
                         help="multi-GPU: SMs left free of GEMM CTAs for the NCCL kernels that overlap them")
-    parser.add_argument("--gather", choices=("all", "root"), default="all")
+    parser.add_argument("--exchange", choices=("ce", "nccl"), default="ce",
+                        help="multi-GPU C exchange: copy-engine pushes over symmetric memory, or NCCL send/recv")
     parser.add_argument("--quick", action="store_true", help="skip the per-precision and cuBLAS tables")
     parser.add_argument("--sweep", choices=("square", "llm", "ragged", "all", "legacy"), default=None,
                         help="instead of the contract line, time every shape of a configuration "

@@ -13,7 +13,13 @@ The reference is single-device (src/benchmark_backends.py selects one
 * with ``BroadcastPipeline`` the B broadcast runs on its own communicator one
   step ahead (double-buffered B), so it too overlaps the GEMMs; the GEMMs are
   then launched on fewer SMs than the device has (``matmul_set_sm_limit``) so
-  that the communication kernels find free SMs while they run.
+  that the communication kernels find free SMs while they run;
+* with ``CopyEngineGather`` the C exchange takes no SM at all: C lives in
+  symmetric memory (every rank maps every peer's C), and each finished chunk
+  is pushed into the peers' C by copy-engine transfers (one cudaMemcpyAsync per
+  peer, on one stream per peer, so the copies of a chunk run side by side); a
+  one-element NCCL all-reduce at the end of the step completes only when every
+  rank's pushes are done, which makes the gathered C safe to read.
 
 Collectives are issued through ``torch.distributed`` (one process per GPU);
 the host-side plan (row ranges, chunking, peer lists) is independent of the
@@ -172,4 +178,79 @@ def pipelined_step(plan: ShardPlan, a_local: torch.Tensor, pipe: BroadcastPipeli
     for work in works:
         work.wait()
     if plan.world > 1:
+        pipe.finish()
+
+
+def _memcpy_d2d(dst: int, src: int, nbytes: int, stream) -> None:
+    """One device-to-device cudaMemcpyAsync (a copy-engine transfer; across GPUs
+    over NVLink when ``dst`` maps a peer's memory).  Raw pointers, no kernel."""
+    from cuda.bindings import runtime as cudart
+
+    (err,) = cudart.cudaMemcpyAsync(dst, src, nbytes, cudart.cudaMemcpyKind.cudaMemcpyDeviceToDevice,
+                                    stream.cuda_stream)
+    if err != cudart.cudaError_t.cudaSuccess:
+        raise RuntimeError(f"cudaMemcpyAsync failed: {err}")
+
+
+class CopyEngineGather:
+    """C exchange of a row-sharded GEMM by copy-engine pushes into the peers' C.
+
+    ``c_full`` must come from ``torch.distributed._symmetric_memory.empty`` on
+    every rank (same shape).  ``post(index, event)`` pushes this rank's chunk
+    ``index`` to every receiver of the plan once ``event`` (recorded after that
+    chunk's GEMM) has completed; ``finish()`` makes the current stream wait for
+    this rank's pushes and runs a one-element all-reduce that completes only when
+    every rank's pushes are done.  Every rank calls ``finish()`` once per step.
+    """
+
+    def __init__(self, plan: ShardPlan, c_full: torch.Tensor, group=None, handle=None, *, copy=None,
+                 new_stream=None):
+        self.plan = plan
+        self.c_full = c_full
+        self.group = group if group is not None else dist.group.WORLD
+        if handle is None:
+            import torch.distributed._symmetric_memory as symm_mem
+
+            handle = symm_mem.rendezvous(c_full, self.group)
+        self.handle = handle
+        self.copy = copy if copy is not None else _memcpy_d2d
+        if new_stream is None:
+            new_stream = lambda: torch.cuda.Stream(device=c_full.device)  # noqa: E731
+        shape, dtype = tuple(c_full.shape), c_full.dtype
+        self.peer_c = {peer: self.handle.get_buffer(peer, shape, dtype) for peer in plan.receivers()}
+        self.streams = {peer: new_stream() for peer in plan.receivers()}
+        self.token = torch.zeros(1, dtype=torch.float32, device=c_full.device)
+        self.row_bytes = c_full.shape[1] * c_full.element_size()
+
+    def post(self, index: int, event) -> None:
+        lo, hi = self.plan.global_chunk(self.plan.rank, index)
+        if hi <= lo:
+            return
+        src = self.c_full.data_ptr() + lo * self.row_bytes
+        for peer, stream in self.streams.items():
+            stream.wait_event(event)
+            self.copy(self.peer_c[peer].data_ptr() + lo * self.row_bytes, src, (hi - lo) * self.row_bytes, stream)
+
+    def finish(self) -> None:
+        current = torch.cuda.current_stream(self.c_full.device)
+        for stream in self.streams.values():
+            current.wait_stream(stream)
+        dist.all_reduce(self.token, group=self.group)
+
+
+def pipelined_step_ce(plan: ShardPlan, a_local: torch.Tensor, pipe: BroadcastPipeline, gather: CopyEngineGather,
+                      gemm: Callable[[torch.Tensor, torch.Tensor, torch.Tensor], None]) -> None:
+    """``pipelined_step`` with the C exchange on copy engines (``CopyEngineGather``)."""
+    if plan.world > 1:
+        pipe.start()
+    start, _ = plan.local_rows
+    c_full = gather.c_full
+    for index, (lo, hi) in enumerate(plan.chunk_ranges[plan.rank]):
+        gemm(a_local[lo:hi], pipe.current, c_full[start + lo:start + hi])
+        if plan.world > 1:
+            event = torch.cuda.Event()
+            event.record()
+            gather.post(index, event)
+    if plan.world > 1:
+        gather.finish()
         pipe.finish()

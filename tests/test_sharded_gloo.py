@@ -147,3 +147,60 @@ def test_row_sharded_gemm_on_gloo_ranks(world, m, chunks, gather, pipelined):
             p.kill()
     assert all(p.exitcode == 0 for p in procs)
     assert dict(results) == {r: True for r in range(world)}
+
+
+class _FakeStream:
+    def wait_event(self, event):
+        pass
+
+
+class _FakeHandle:
+    """Stands in for a symmetric-memory handle: rank p's buffer is ``buffers[p]``."""
+
+    def __init__(self, buffers):
+        self.buffers = buffers
+
+    def get_buffer(self, peer, shape, dtype):
+        buffer = self.buffers[peer]
+        assert tuple(buffer.shape) == tuple(shape) and buffer.dtype == dtype
+        return buffer
+
+
+def _memmove_copy(dst, src, nbytes, stream):
+    import ctypes
+
+    ctypes.memmove(dst, src, nbytes)
+
+
+@pytest.mark.parametrize("world,m,chunks,gather", [(2, 37, 3, "all"), (3, 64, 4, "all"), (4, 9, 8, "all"),
+                                                   (3, 50, 2, "root"), (8, 100, 3, "all")])
+def test_copy_engine_gather_places_every_chunk(world, m, chunks, gather):
+    """CopyEngineGather's row arithmetic: after every rank has posted every chunk,
+    each receiver's C holds every sender's rows at the right place (all ranks in one
+    process, host buffers standing in for the peers' mapped C, memmove for the copy)."""
+    from sharded import CopyEngineGather
+
+    n = 5
+    expected = torch.arange(m * n, dtype=torch.float32).reshape(m, n)
+    buffers = []
+    plans = [ShardPlan(m, 3, n, world, r, chunks=chunks, gather=gather) for r in range(world)]
+    for r, plan in enumerate(plans):
+        c = torch.full((m, n), -1.0)
+        lo, hi = plan.local_rows
+        c[lo:hi] = expected[lo:hi]
+        buffers.append(c)
+    handle = _FakeHandle(buffers)
+    gathers = [CopyEngineGather(plan, buffers[r], group=object(), handle=handle, copy=_memmove_copy,
+                                new_stream=_FakeStream) for r, plan in enumerate(plans)]
+    for index in range(plans[0].chunk_count):
+        for g in gathers:
+            g.post(index, event=None)
+    for r in range(world):
+        if gather == "all" or r == 0:
+            assert torch.equal(buffers[r], expected), r
+        else:
+            lo, hi = plans[r].local_rows
+            assert torch.equal(buffers[r][lo:hi], expected[lo:hi])
+            outside = torch.ones(m, dtype=torch.bool)
+            outside[lo:hi] = False
+            assert torch.all(buffers[r][outside] == -1.0)
