@@ -13,7 +13,8 @@
  * Implementation ids (the reference's ids 0-6 name kernels this library does
  * not contain and are rejected with an error):
  *   7  "tcgen05"  TF32 (1), FP16 (2), BF16 (3): tcgen05.mma with TMEM accumulators
- *   8  "ffma"     FP32 pedantic (0): register-blocked FFMA, no TF32 anywhere
+ *   8  "ffma"     FP32 pedantic (0): register-blocked FFMA, no TF32 anywhere (TMA-staged
+ *                 operands when they are 16-byte aligned)
  * Precision ids follow src/precision.py:8-10: 0 fp32, 1 tf32, 2 fp16, 3 bf16.
  */
 #ifndef B200_MATMUL_H
@@ -53,11 +54,13 @@ int matmul_destroy(void *context, char *error, size_t error_size);
 
 /* Replaces matmul_launch (src/matmul.cu:349-479): C = A * B on `stream`
  * (a cudaStream_t), asynchronous, CUDA-graph capturable.  TF32 inputs are
- * rounded to nearest-even before the tensor-core product; unaligned or
- * TMA-incompatible operands are repacked into stream-ordered scratch first.
+ * rounded to nearest-even before the tensor-core product, by the TMA loads of
+ * TFLOAT32 tensor maps; operands TMA cannot address (base not 16-byte aligned,
+ * or a row pitch that is not a multiple of 16 bytes) are repacked into
+ * stream-ordered scratch first.
  * TF32 problems with m*k*n <= 2^25 run on the FFMA kernel with each K tile of
  * the operands rounded to TF32 (nearest even) in shared memory: the same exact
- * products, accumulated in FP32, without the operand pre-pass. */
+ * products, accumulated in FP32, without the tensor-core start-up. */
 int matmul_launch(void *context, int implementation, int precision,
                   const void *a, const void *b, float *c, int m, int k, int n,
                   void *stream, char *error, size_t error_size);
@@ -121,7 +124,9 @@ int matmul_set_sm_limit(void *context, int sms, char *error, size_t error_size);
  * matmul_device_status), writes NaN over every output element it did not
  * finish, releases its tensor memory and returns, so that the context stays
  * usable and an FP64 check of C fails.  For watchdog tests and for callers that
- * want a kernel to give up sooner; the FFMA kernels have no such waits. */
+ * want a kernel to give up sooner.  The FFMA kernel's TMA-staged 128 x 128 tile
+ * (16-byte aligned operands) bounds its stage waits the same way; its cp.async
+ * forms have no waits. */
 int matmul_set_wait_limit(void *context, unsigned long long nanoseconds, char *error, size_t error_size);
 
 /* No counterpart in the reference.  Same arguments, result and error convention
@@ -129,19 +134,18 @@ int matmul_set_wait_limit(void *context, unsigned long long nanoseconds, char *e
  * for callers that must not call cudaMalloc or a stream-ordered allocator --
  * typically a process whose framework has already reserved nearly all device
  * memory in its own pool, where one more allocation at launch time would fail
- * or force that pool to give memory back.  The TF32 rounding copies and the repacked copies of unaligned operands
- * that matmul_launch places in pool memory go instead into one fixed 32 MiB
+ * or force that pool to give memory back.  The repacked copies of unaligned
+ * operands that matmul_launch places in pool memory go instead into one fixed 32 MiB
  * array compiled into the library (every GPU that loads the library holds it
  * until the process exits).  A problem whose copies need more than 32 MiB is
  * rejected with "matmul_launch_noalloc: this problem needs N bytes of scratch,
  * more than the fixed ...".  The rule is the one matmul_launch applies, whatever
- * kernel the launch plan then picks (split K included): a TF32 problem with
- * m*k*n > 2^25 copies both operands, 4*m*k' + 4*n*k' bytes with k' = k rounded
- * up to 4; an FP16/BF16 operand whose base address is not 16-byte aligned, or
- * whose row pitch (2*k bytes for A, 2*n for B) is not a multiple of 16, is
- * repacked into m*k'' (A) or k*n'' (B) 2-byte elements with k'', n'' rounded up
- * to 8; each copy is rounded up to 256 bytes.  TF32 problems with m*k*n <= 2^25
- * and aligned FP16/BF16 operands need no scratch.  The first call through a
+ * kernel the launch plan then picks (split K included): an operand whose base
+ * address is not 16-byte aligned, or whose row pitch (e*k bytes for A, e*n for
+ * B, e = 4 for TF32 and 2 for FP16/BF16) is not a multiple of 16, is repacked
+ * into m*k' (A) or k*n' (B) elements with k', n' rounded up to 16/e; each copy is
+ * rounded up to 256 bytes.  Aligned operands, and TF32 problems with
+ * m*k*n <= 2^25 (FFMA kernel), need no scratch.  The first call through a
  * context looks up the array's device address with that context's device
  * current and keeps it in the context; make that first call before any stream
  * capture (a context does not survive a device reset; create a new one after

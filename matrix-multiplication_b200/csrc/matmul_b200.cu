@@ -17,6 +17,7 @@
 #include <new>
 
 #include "ffma_gemm.cuh"
+#include "ffma_tma.cuh"
 #include "pack.cuh"
 #include "tc_gemm.cuh"
 #include "tc2_gemm.cuh"
@@ -124,14 +125,15 @@ int64_t round_up(int64_t x, int64_t to)
 }
 
 bool encode_2d(const Context *ctx, CUtensorMap *map, CUtensorMapDataType type, const void *base, uint64_t inner,
-               uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer)
+               uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+               CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B)
 {
     const cuuint64_t dims[2] = {inner, outer};
     const cuuint64_t strides[1] = {row_bytes};
     const cuuint32_t box[2] = {box_inner, box_outer};
     const cuuint32_t elem_strides[2] = {1, 1};
     const CUresult r = ctx->encode(map, type, 2, const_cast<void *>(base), dims, strides, box, elem_strides,
-                                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                   CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
@@ -192,37 +194,10 @@ cudaError_t launch_pdl_cluster_z(void (*kernel)(Params...), dim3 grid, dim3 bloc
 }
 
 
-// TF32 B: dst (n x ld) = rounded transpose of src (k x n).
-// Both TF32 operands in one launch: rounded A (m x lda) and rounded, transposed B
-// (n x ldb), each into 16-byte aligned scratch.
-cudaError_t prepare_tf32(const Context *ctx, const float *a, float *a_dst, int64_t m, int64_t k, int64_t lda,
-                         const float *b, float *b_dst, int64_t n, int64_t ldb, cudaStream_t stream)
-{
-    Tf32Prep prep{};
-    prep.a = a;
-    prep.a_dst = a_dst;
-    prep.b = b;
-    prep.b_dst = b_dst;
-    prep.m = m;
-    prep.k = k;
-    prep.n = n;
-    prep.lda = lda;
-    prep.ldb = ldb;
-    prep.a_vec = aligned16(a) && lda == k ? 1 : 0;
-    prep.b_vec = aligned16(b) && n % 4 == 0 ? 1 : 0;
-    const int64_t a_work = prep.a_vec ? m * k / 4 : m * lda;
-    const int64_t a_cap = 4LL * ctx->sm_count, b_cap = 8LL * ctx->sm_count;
-    int64_t a_blocks = (a_work + 255) / 256;
-    a_blocks = a_blocks < 1 ? 1 : a_blocks > a_cap ? a_cap : a_blocks;
-    int64_t b_blocks = ((n + TP_TILE - 1) / TP_TILE) * ((ldb + TP_TILE - 1) / TP_TILE);
-    b_blocks = b_blocks < 1 ? 1 : b_blocks > b_cap ? b_cap : b_blocks;
-    prep.a_blocks = static_cast<int>(a_blocks);
-    return launch_pdl(tf32_prepare_kernel, dim3(static_cast<unsigned int>(a_blocks + b_blocks)), dim3(256), 0,
-                      stream, prep);
-}
-
-// FP16/BF16 operands TMA cannot read in place, repacked into 16-byte aligned
-// scratch in one launch (an operand with `direct` set is skipped).
+// Operands TMA cannot read in place (base not 16-byte aligned, or a row pitch
+// that is not a multiple of 16 bytes), repacked into 16-byte aligned scratch in
+// one launch (an operand with `direct` set is skipped).  TF32 operands are copied
+// as FP32 words: the TMA loads round them.
 template <typename T>
 cudaError_t pack_operands(const Context *ctx, const void *a, bool a_direct, void *a_dst, int64_t m, int64_t k,
                           int64_t lda, const void *b, bool b_direct, void *b_dst, int64_t n, int64_t ldb,
@@ -401,26 +376,21 @@ cudaError_t launch_skinny_np(int np, const CUtensorMap &mbt, const CUtensorMap &
 }
 
 // m <= 64: C^T = B^T A^T with N on the MMA's 128-row side (tc_skinny.cuh).  The
-// operands are already in TMA-ready form (a_op: m x lda; b_op: k x ldb, or for
-// TF32 the rounded transpose n x ldb).
+// operands are already in TMA-ready form (a_op: m x lda; b_op: k x ldb).
 int launch_skinny(Context *ctx, int prec, const void *a_op, int64_t lda, const void *b_op, int64_t ldb,
-                  bool b_transposed, float *c, int m, int k, int n, cudaStream_t stream, char *error,
-                  size_t error_size)
+                  float *c, int m, int k, int n, cudaStream_t stream, char *error, size_t error_size)
 {
     const int elem = prec == kPrecTf32 ? 4 : 2;
     const uint32_t bk = TC_ROW_BYTES / elem;
     const int np = m <= 16 ? 16 : m <= 32 ? 32 : 64;
-    const CUtensorMapDataType type = prec == kPrecTf32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+    const CUtensorMapDataType type = prec == kPrecTf32 ? CU_TENSOR_MAP_DATA_TYPE_TFLOAT32
                                      : prec == kPrecBf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                          : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     alignas(64) CUtensorMap map_bt, map_at;
-    bool ok;
-    if (b_transposed)
-        ok = encode_2d(ctx, &map_bt, type, b_op, static_cast<uint64_t>(k), static_cast<uint64_t>(n),
-                       static_cast<uint64_t>(ldb) * elem, bk, SK_BM);
-    else
-        ok = encode_2d(ctx, &map_bt, type, b_op, static_cast<uint64_t>(n), static_cast<uint64_t>(k),
-                       static_cast<uint64_t>(ldb) * elem, TC_ROW_BYTES / elem, bk);
+    const CUtensorMapSwizzle b_swizzle =
+        prec == kPrecTf32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
+    bool ok = encode_2d(ctx, &map_bt, type, b_op, static_cast<uint64_t>(n), static_cast<uint64_t>(k),
+                        static_cast<uint64_t>(ldb) * elem, TC_ROW_BYTES / elem, SK_B_ROWS, b_swizzle);
     ok = ok && encode_2d(ctx, &map_at, type, a_op, static_cast<uint64_t>(k), static_cast<uint64_t>(m),
                          static_cast<uint64_t>(lda) * elem, bk, static_cast<uint32_t>(np));
     if (!ok) {
@@ -468,15 +438,16 @@ int launch_tcgen05(Context *ctx, int prec, const void *a, const void *b, float *
                                 stream, error, error_size);
     const int elem = prec == kPrecTf32 ? 4 : 2;
     const int64_t align_elems = 16 / elem;
-    // TMA needs 16-byte aligned bases and row pitches; TF32 always needs rounding.
-    const bool a_direct = prec != kPrecTf32 && aligned16(a) && (static_cast<int64_t>(k) * elem) % 16 == 0;
-    const bool b_direct = prec != kPrecTf32 && aligned16(b) && (static_cast<int64_t>(n) * elem) % 16 == 0;
-    const bool b_transposed = prec == kPrecTf32;   // TF32 B goes K-major (n x ldb)
+    // TMA needs 16-byte aligned bases and row pitches; operands without them are
+    // repacked.  TF32 operands are read as FP32 words through TFLOAT32 tensor maps,
+    // whose loads round each word to TF32 (nearest even, the reference's
+    // round_tf32_even), so TF32 needs no pass of its own.
+    const bool a_direct = aligned16(a) && (static_cast<int64_t>(k) * elem) % 16 == 0;
+    const bool b_direct = aligned16(b) && (static_cast<int64_t>(n) * elem) % 16 == 0;
     const int64_t lda = a_direct ? k : round_up(k, align_elems);
-    const int64_t ldb = b_direct ? n : b_transposed ? round_up(k, align_elems) : round_up(n, align_elems);
-    const int64_t b_rows = b_transposed ? n : k;
+    const int64_t ldb = b_direct ? n : round_up(n, align_elems);
     const size_t a_bytes = a_direct ? 0 : static_cast<size_t>(round_up(static_cast<int64_t>(m) * lda * elem, 256));
-    const size_t b_bytes = b_direct ? 0 : static_cast<size_t>(round_up(b_rows * ldb * elem, 256));
+    const size_t b_bytes = b_direct ? 0 : static_cast<size_t>(round_up(static_cast<int64_t>(k) * ldb * elem, 256));
 
     void *scratch = nullptr;
     if (a_bytes + b_bytes && fixed_scratch) {
@@ -498,18 +469,12 @@ int launch_tcgen05(Context *ctx, int prec, const void *a, const void *b, float *
     void *pooled = fixed_scratch ? nullptr : scratch;
     const void *a_op = a_direct ? a : scratch;
     const void *b_op = b_direct ? b : static_cast<uint8_t *>(scratch) + a_bytes;
-    if (prec == kPrecTf32) {
-        const cudaError_t st = prepare_tf32(ctx, static_cast<const float *>(a), static_cast<float *>(const_cast<void *>(a_op)),
-                                            m, k, lda, static_cast<const float *>(b),
-                                            static_cast<float *>(const_cast<void *>(b_op)), n, ldb, stream);
-        if (st != cudaSuccess) {
-            if (pooled)
-                cudaFreeAsync(pooled, stream);
-            return fail(error, error_size, "kernel launch", cudaGetErrorString(st));
-        }
-    } else {
+    {
         const cudaError_t st =
-            prec == kPrecBf16
+            prec == kPrecTf32
+                ? pack_operands<float>(ctx, a, a_direct, const_cast<void *>(a_op), m, k, lda, b, b_direct,
+                                       const_cast<void *>(b_op), n, ldb, stream)
+            : prec == kPrecBf16
                 ? pack_operands<__nv_bfloat16>(ctx, a, a_direct, const_cast<void *>(a_op), m, k, lda, b, b_direct,
                                                const_cast<void *>(b_op), n, ldb, stream)
                 : pack_operands<__half>(ctx, a, a_direct, const_cast<void *>(a_op), m, k, lda, b, b_direct,
@@ -522,8 +487,7 @@ int launch_tcgen05(Context *ctx, int prec, const void *a, const void *b, float *
     }
 
     if (m <= kSkinnyMaxM) {
-        const int rc = launch_skinny(ctx, prec, a_op, lda, b_op, ldb, b_transposed, c, m, k, n, stream, error,
-                                     error_size);
+        const int rc = launch_skinny(ctx, prec, a_op, lda, b_op, ldb, c, m, k, n, stream, error, error_size);
         if (pooled)
             cudaFreeAsync(pooled, stream);
         return rc;
@@ -534,7 +498,7 @@ int launch_tcgen05(Context *ctx, int prec, const void *a, const void *b, float *
     const bool pair = kernel_n == 0 || kernel_n == TC2W_BN;
     const int tile_m = pair ? TC2_BM : TC_BM;
     const int tile_n = kernel_n == 0 ? TC2_BN : kernel_n;
-    const CUtensorMapDataType type = prec == kPrecTf32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+    const CUtensorMapDataType type = prec == kPrecTf32 ? CU_TENSOR_MAP_DATA_TYPE_TFLOAT32
                                      : prec == kPrecBf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                          : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     const uint32_t bk = TC_ROW_BYTES / elem;
@@ -544,12 +508,9 @@ int launch_tcgen05(Context *ctx, int prec, const void *a, const void *b, float *
     const int a_box_rows = pair || m >= TC_BM ? TC_BM : static_cast<int>(round_up(m, 16));
     bool ok = encode_2d(ctx, &map_a, type, a_op, static_cast<uint64_t>(k), static_cast<uint64_t>(m),
                         static_cast<uint64_t>(lda) * elem, bk, static_cast<uint32_t>(a_box_rows));
-    if (b_transposed)
-        ok = ok && encode_2d(ctx, &map_b, type, b_op, static_cast<uint64_t>(k), static_cast<uint64_t>(n),
-                             static_cast<uint64_t>(ldb) * elem, bk, pair ? TC2_HALF : tile_n);
-    else
-        ok = ok && encode_2d(ctx, &map_b, type, b_op, static_cast<uint64_t>(n), static_cast<uint64_t>(k),
-                             static_cast<uint64_t>(ldb) * elem, TC_ROW_BYTES / elem, bk);
+    ok = ok && encode_2d(ctx, &map_b, type, b_op, static_cast<uint64_t>(n), static_cast<uint64_t>(k),
+                         static_cast<uint64_t>(ldb) * elem, TC_ROW_BYTES / elem, bk,
+                         prec == kPrecTf32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B);
     const bool c_direct = !(aligned16(c) && n % 4 == 0);
     if (ok && !c_direct)
         ok = encode_2d(ctx, &map_c, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, c, static_cast<uint64_t>(n),
@@ -686,7 +647,7 @@ cudaError_t launch_ffma_plan(const FfmaPlan &plan, const float *a, const float *
 
 // TF32 problems this small run on the FFMA kernel with each K tile rounded to
 // TF32 in shared memory (the TF32 products are exact in FP32): below about 320^3 the
-// tensor-core path's operand pre-pass and start-up cost more than the FMAs
+// tensor-core path's start-up costs more than the FMAs
 // (measured: 64^3-256^3 TF32 at 5.4-7.8 us on the tensor cores, 2.9-4.4 us here).
 bool tf32_on_ffma(int m, int k, int n)
 {
@@ -708,13 +669,54 @@ int launch_ffma_tf32(const Context *ctx, const float *a, const float *b, float *
     return 0;
 }
 
+// The 128 x 128 FFMA tile with TMA-staged operands (ffma_tma.cuh); needs 16-byte
+// aligned operands and row pitches, which the caller has checked.
+cudaError_t launch_ffma_tma(const Context *ctx, const float *a, const float *b, float *c, int m, int k, int n,
+                            int splits, bool vec_c, cudaStream_t stream, bool &encoded)
+{
+    alignas(64) CUtensorMap map_a, map_b;
+    encoded = encode_2d(ctx, &map_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a, static_cast<uint64_t>(k),
+                        static_cast<uint64_t>(m), static_cast<uint64_t>(k) * 4, FT_BK, FT_BM) &&
+              encode_2d(ctx, &map_b, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, b, static_cast<uint64_t>(n),
+                        static_cast<uint64_t>(k), static_cast<uint64_t>(n) * 4, 32, FT_BK);
+    if (!encoded)
+        return cudaSuccess;
+    FtParams params{};
+    params.m = m;
+    params.n = n;
+    params.k = k;
+    params.c = c;
+    params.wait_limit_ns = wait_limit(ctx);
+    const int64_t gx = (static_cast<int64_t>(n) + FT_BN - 1) / FT_BN;
+    const int64_t gy = (static_cast<int64_t>(m) + FT_BM - 1) / FT_BM;
+    const dim3 grid(static_cast<unsigned int>(gx < 65535 ? gx : 65535),
+                    static_cast<unsigned int>(gy < 65535 ? gy : 65535), static_cast<unsigned int>(splits));
+    if (vec_c)
+        return launch_pdl_cluster_z(ffma_tma_kernel<true>, grid, dim3(FT_THREADS), FT_SMEM, splits, stream, map_a,
+                                    map_b, params);
+    return launch_pdl_cluster_z(ffma_tma_kernel<false>, grid, dim3(FT_THREADS), FT_SMEM, splits, stream, map_a,
+                                map_b, params);
+}
+
 int launch_ffma(const Context *ctx, const float *a, const float *b, float *c, int m, int k, int n,
                 cudaStream_t stream, char *error, size_t error_size)
 {
-    // 16-byte copies when both operands' rows are 16-byte aligned, 4-byte copies otherwise.
+    // 16-byte aligned operands: the 128 x 128 tile is staged by TMA, the 32 x 32
+    // tile by 16-byte cp.async; otherwise 4-byte cp.async copies.
     const bool vec_ab = aligned16(a) && k % 4 == 0 && aligned16(b) && n % 4 == 0;
     const bool vec_c = aligned16(c) && n % 4 == 0;
     const FfmaPlan plan = choose_ffma_plan(m, k, n, ctx->sm_count, ctx->ffma_resident);
+    if (vec_ab && plan.tile == 0) {
+        bool encoded = false;
+        const cudaError_t st = launch_ffma_tma(ctx, a, b, c, m, k, n, plan.splits, vec_c, stream, encoded);
+        if (!encoded) {
+            cudaGetLastError();
+            return fail(error, error_size, "matmul_launch", "cuTensorMapEncodeTiled rejected an operand");
+        }
+        if (st != cudaSuccess)
+            return fail(error, error_size, "kernel launch", cudaGetErrorString(st));
+        return 0;
+    }
     const cudaError_t st = vec_ab ? launch_ffma_plan<true>(plan, a, b, c, m, k, n, vec_c, stream)
                                   : launch_ffma_plan<false>(plan, a, b, c, m, k, n, vec_c, stream);
     if (st != cudaSuccess)
@@ -783,16 +785,17 @@ extern "C" int matmul_kernel_info(int implementation, int precision, char *json,
             "\"small_tf32\":\"ffma_tf32_rne when m*k*n<=2^25\"}",
             kPrecisionNames[precision], TC2_BM, TC2_BN, TC_ROW_BYTES / elem, TC_THREADS, TC2_HALF, TC2_BN, TC2_HALF,
             TC2_BN, TC2_STAGES, precision == kPrecTf32 ? "tf32" : "f16", TC2_BM, TC2_BN, 32 / elem,
-            TC_TMEM_COLUMNS, kRasterGroupMPair, precision == kPrecTf32 ? "rne_prepass" : "none",
-            precision == kPrecTf32 ? "k_major_rounded_transpose" : "mn_major_tma", TC_BM, TcTile<256>::kStages,
+            TC_TMEM_COLUMNS, kRasterGroupMPair, precision == kPrecTf32 ? "rne by the TMA loads (TFLOAT32 tensor maps)" : "none",
+            precision == kPrecTf32 ? "mn_major_tma_sw128_atom32B" : "mn_major_tma_sw128", TC_BM, TcTile<256>::kStages,
             TcTile<128>::kStages, TcTile<64>::kStages, kRasterGroupM, TC2W_BN, Tc2Tile<TC2W_BN>::kStages, SK_BM);
     } else {
         written = std::snprintf(
             json, json_size,
             "{\"implementation\":\"ffma\",\"precision\":\"fp32\",\"tile_m\":%d,\"tile_n\":%d,"
             "\"tile_k\":%d,\"threads\":%d,\"warp_tile_m\":%d,\"warp_tile_n\":%d,\"microtile_m\":8,"
-            "\"microtile_n\":8,\"buffering\":%d,\"load_method\":\"cp_async_zero_fill\","
-            "\"copy_bytes\":\"16 when A and B rows are 16-byte aligned, else 4\","
+            "\"microtile_n\":8,\"buffering\":%d,\"load_method\":\"tma_sw128 when A and B rows are 16-byte "
+            "aligned, else cp_async_zero_fill\","
+            "\"copy_bytes\":\"TMA boxes (aligned 128 x 128 tile), 16-byte cp.async (aligned 32 x 32 tile), else 4\","
             "\"tensor_cores\":false,\"fma\":\"ffma2_rn_packed_fp32x2\",\"blocks_per_sm\":2,"
             "\"small_tiles\":[[32,32,4,4]],\"split_k\":\"cluster_1x1xS_dsmem_reduce\","
             "\"max_splits\":%d,\"plan_choice\":\"cost_model_busiest_sm\"}",
@@ -904,6 +907,15 @@ extern "C" void *matmul_create(int device, char *error, size_t error_size)
         }
     }
 #undef B200_FFMA_KERNEL
+    for (const void *kernel : {reinterpret_cast<const void *>(&ffma_tma_kernel<true>),
+                               reinterpret_cast<const void *>(&ffma_tma_kernel<false>)}) {
+        st = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FT_SMEM);
+        if (st != cudaSuccess) {
+            delete ctx;
+            fail_cuda(error, error_size, "cudaFuncSetAttribute", st);
+            return nullptr;
+        }
+    }
     for (const auto &kernel : ffma_kernels) {
         st = cudaFuncSetAttribute(kernel.first, cudaFuncAttributeMaxDynamicSharedMemorySize, kernel.second);
         if (st != cudaSuccess) {
@@ -1092,11 +1104,12 @@ extern "C" int matmul_plan(void *opaque, int implementation, int precision, int 
         written = std::snprintf(json, json_size,
                                 "{\"kernel\":\"ffma_async\",\"tile_m\":%d,\"tile_n\":%d,\"threads\":%d,"
                                 "\"splits\":%d,\"cluster\":[1,1,%d],\"grid\":[%lld,%lld,%d],"
-                                "\"vector_loads_if_aligned\":%s}",
+                                "\"vector_loads_if_aligned\":%s,\"staging_if_aligned\":\"%s\"}",
                                 o.bm, o.bn, o.warps * 32, plan.splits, plan.splits,
                                 static_cast<long long>((n + o.bn - 1) / o.bn),
                                 static_cast<long long>((m + o.bm - 1) / o.bm), plan.splits,
-                                k % 4 == 0 && n % 4 == 0 ? "true" : "false");
+                                k % 4 == 0 && n % 4 == 0 ? "true" : "false",
+                                k % 4 == 0 && n % 4 == 0 ? (plan.tile == 0 ? "tma" : "cp_async16") : "cp_async4");
     } else if (precision == kPrecTf32 && tf32_on_ffma(m, k, n)) {
         const FfmaPlan plan = choose_ffma_plan(m, k, n, ctx->sm_count, ctx->ffma_resident, 2u);
         written = std::snprintf(json, json_size,

@@ -85,10 +85,40 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity)
     return done != 0;
 }
 
+// Non-blocking test of the phase with the given parity (no suspension).
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity)
+{
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// Limits below this are watchdog settings (matmul_set_wait_limit): they poll
+// with test_wait, which never suspends, so that even a wait shorter than
+// try_wait's own suspension (one TMA stage) can run out.
+constexpr uint64_t kShortWaitNs = 1000000ull;
+
 // Waits until the phase with the given parity has completed.  Returns false
 // (without waiting further) once `limit_ns` has passed.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint64_t limit_ns = kWaitLimitNs)
 {
+    if (limit_ns < kShortWaitNs) {
+        const uint64_t start = global_timer_ns();
+        for (;;) {
+            if (mbar_test_wait(bar, parity))
+                return true;
+            // %globaltimer advances in steps of up to a microsecond: a limit below that
+            // allows one test.
+            if (limit_ns < 1000u || global_timer_ns() - start > limit_ns)
+                return false;
+        }
+    }
     if (mbar_try_wait(bar, parity))
         return true;
     // try_wait itself suspends the thread for a while before it reports "not yet",
@@ -431,16 +461,36 @@ __device__ __forceinline__ void tmem_load_16cols(uint32_t taddr, uint32_t (&v)[1
 
 // Shared-memory matrix descriptor for tcgen05.mma (sm_100 format, version 1):
 // start address, leading- and stride-dimension byte offsets (all >> 4) and the
-// 128-byte swizzle layout (type 2 in bits 61-63).
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes)
+// swizzle layout in bits 61-63: 2 = 128-byte swizzle (16-byte chunks XOR row % 8
+// over 8 rows of 128 bytes), 1 = 128-byte swizzle with 32-byte atoms (32-byte
+// chunks XOR row % 4 over 4 rows of 128 bytes), the form an MN-major TF32
+// operand takes.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes,
+                                              uint32_t layout_type)
 {
     uint64_t desc = 0;
     desc |= static_cast<uint64_t>((addr & 0x3FFFFu) >> 4);
     desc |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
     desc |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
     desc |= 1ull << 46;
-    desc |= 2ull << 61;
+    desc |= static_cast<uint64_t>(layout_type & 7u) << 61;
     return desc;
+}
+
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes)
+{
+    return smem_desc(addr, lbo_bytes, sbo_bytes, 2u);
+}
+
+// Descriptor of an MN-major operand staged as boxes of 128-byte rows (one row
+// per k, kBK rows per box), consecutive boxes `box_bytes` apart along M/N.
+// FP16/BF16: 128-byte swizzle, 8-row atoms (stride-dimension offset 1024);
+// TF32: 32-byte-atom swizzle, 4-row atoms (offset 512).  The leading-dimension
+// offset is the distance between boxes.
+template <bool TF32>
+__device__ __forceinline__ uint64_t smem_desc_mn(uint32_t addr, uint32_t box_bytes)
+{
+    return TF32 ? smem_desc(addr, box_bytes, 512u, 1u) : smem_desc(addr, box_bytes, 1024u, 2u);
 }
 
 } // namespace b200

@@ -88,8 +88,7 @@ tc2_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
     constexpr int kNB = TC_ROW_BYTES / kElem;          // MN-major B box width (64)
     constexpr int kBBoxes = TC2_HALF / kNB;            // 2 boxes per CTA half (MN-major B)
     constexpr uint32_t kBBoxBytes = kBK * TC_ROW_BYTES;
-    constexpr bool kBKMajor = kTF32;
-    constexpr uint32_t kIdesc = tc_instr_desc(FMT, kBKMajor, TC2_BM, 256);
+    constexpr uint32_t kIdesc = tc_instr_desc(FMT, false, TC2_BM, 256);   // B MN-major in every format
     constexpr uint32_t kBHalfBytes = TC2_HALF * TC_ROW_BYTES;         // one 128-column B half of a CTA
     constexpr uint32_t kStageTx = 2u * (TC2_A_STAGE + kBStage);       // both CTAs
 
@@ -171,14 +170,9 @@ tc2_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
 #pragma unroll
                     for (int h = 0; h < kHalves; ++h) {
                         const uint32_t s_bh = s_b + stage * kBStage + h * kBHalfBytes;
-                        if constexpr (kBKMajor) {
-                            tma_load_2d_pair(s_bh, &map_b, fb, kb * kBK, b_col + h * 256);
-                        } else {
 #pragma unroll
-                            for (int j = 0; j < kBBoxes; ++j)
-                                tma_load_2d_pair(s_bh + j * kBBoxBytes, &map_b, fb, b_col + h * 256 + j * kNB,
-                                                 kb * kBK);
-                        }
+                        for (int j = 0; j < kBBoxes; ++j)
+                            tma_load_2d_pair(s_bh + j * kBBoxBytes, &map_b, fb, b_col + h * 256 + j * kNB, kb * kBK);
                     }
                     filled |= 1u << stage;
                     fill_parity = (fill_parity & ~(1u << stage)) | (phase << stage);
@@ -204,12 +198,12 @@ tc2_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
             // Loop-invariant descriptor halves: only the start-address field (bits 0-13,
             // address >> 4) moves between stages and K slices, so the issue loop adds.
             const uint64_t a_desc0 = smem_desc_sw128(s_a, 16, 1024);
-            const uint64_t b_desc0 = kBKMajor ? smem_desc_sw128(s_b, 16, 1024) : smem_desc_sw128(s_b, kBBoxBytes, 1024);
+            const uint64_t b_desc0 = smem_desc_mn<kTF32>(s_b, kBBoxBytes);
             constexpr uint64_t kADescStage = TC2_A_STAGE >> 4;
             constexpr uint64_t kBDescStage = kBStage >> 4;
             constexpr uint64_t kBDescHalf = kBHalfBytes >> 4;
             constexpr uint64_t kADescK = 32 >> 4;
-            constexpr uint64_t kBDescK = kBKMajor ? (32 >> 4) : ((kMmaK * TC_ROW_BYTES) >> 4);
+            constexpr uint64_t kBDescK = (kMmaK * TC_ROW_BYTES) >> 4;
             // The MMAs of one K block for one 256-column half of the accumulator.
             auto issue_half = [&](uint32_t d_tmem, int s, int h, int kb) {
                 const uint64_t a_desc = a_desc0 + static_cast<uint64_t>(s) * kADescStage;

@@ -19,11 +19,12 @@
 //               is not TMA-compatible, store directly with bounds checks).
 //               Runs one tile behind the MMA thanks to the two accumulators.
 //
-// A is K-major in shared memory.  For FP16/BF16, B stays row-major (N
-// contiguous), i.e. the MN-major operand form of the instruction descriptor,
-// so neither operand is transposed in memory.  TF32 operands are rounded by a
-// pre-pass anyway, and that pass also transposes B so that TF32 B is K-major
-// like A (MN-major TF32 would need the 32-byte-atom swizzle).  Tiles are
+// A is K-major in shared memory.  B stays row-major (N contiguous), i.e. the
+// MN-major operand form of the instruction descriptor, so neither operand is
+// transposed in memory: FP16/BF16 boxes use the 128-byte swizzle, TF32 boxes
+// the 128-byte swizzle with 32-byte atoms that an MN-major TF32 operand needs.
+// TF32 operands are FP32 words in memory; the TMA loads of their TFLOAT32
+// tensor maps round each to TF32 (nearest even) on the way in.  Tiles are
 // visited persistently (tile += gridDim.x) in groups of `group_m` M-blocks so
 // that concurrently running CTAs share A and B panels in L2.
 //
@@ -167,8 +168,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     constexpr int kNB = TC_ROW_BYTES / kElem;          // B box width in elements (64 or 32)
     constexpr int kBBoxes = BN / kNB;                  // MN-major B boxes per stage
     constexpr uint32_t kBBoxBytes = kBK * TC_ROW_BYTES;  // bytes per B column block
-    constexpr bool kBKMajor = kTF32;                     // TF32 B arrives transposed
-    constexpr uint32_t kIdesc = tc_instr_desc(FMT, kBKMajor, TC_BM, BN);
+    // B is read MN-major straight from its row-major rows (N contiguous) in every
+    // format; TF32 in 32-byte-atom swizzled boxes (smem_desc_mn).
+    constexpr uint32_t kIdesc = tc_instr_desc(FMT, false, TC_BM, BN);
     // Split K: this CTA's 128 x BN FP32 partial, then up to S-1 received row
     // slices, in the operand ring and the epilogue staging area behind it.
     constexpr uint32_t kPartialRowBytes = BN * 4;
@@ -250,15 +252,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                     }
                     mbar_arrive_expect_tx(full_bar(stage), p.a_box_rows * TC_ROW_BYTES + kBStage);
                     tma_load_2d(s_a + stage * kAStage, &map_a, full_bar(stage), kb * kBK, mb * TC_BM);
-                    if constexpr (kBKMajor) {
-                        // B^T tile: BN rows (n) x 128 bytes (k), one box.
-                        tma_load_2d(s_b + stage * kBStage, &map_b, full_bar(stage), kb * kBK, nb * BN);
-                    } else {
 #pragma unroll
-                        for (int j = 0; j < kBBoxes; ++j)
-                            tma_load_2d(s_b + stage * kBStage + j * kBBoxBytes, &map_b, full_bar(stage),
-                                        nb * BN + j * kNB, kb * kBK);
-                    }
+                    for (int j = 0; j < kBBoxes; ++j)
+                        tma_load_2d(s_b + stage * kBStage + j * kBBoxBytes, &map_b, full_bar(stage),
+                                    nb * BN + j * kNB, kb * kBK);
                     filled |= 1u << stage;
                     fill_parity = (fill_parity & ~(1u << stage)) | (phase << stage);
                     if (++stage == kStages) {
@@ -282,11 +279,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             // Loop-invariant descriptor halves: only the start-address field (bits 0-13,
             // address >> 4) moves between stages and K slices, so the issue loop adds.
             const uint64_t a_desc0 = smem_desc_sw128(s_a, 16, 1024);
-            const uint64_t b_desc0 = kBKMajor ? smem_desc_sw128(s_b, 16, 1024) : smem_desc_sw128(s_b, kBBoxBytes, 1024);
+            const uint64_t b_desc0 = smem_desc_mn<kTF32>(s_b, kBBoxBytes);
             constexpr uint64_t kADescStage = kAStage >> 4;
             constexpr uint64_t kBDescStage = kBStage >> 4;
             constexpr uint64_t kADescK = 32 >> 4;
-            constexpr uint64_t kBDescK = kBKMajor ? (32 >> 4) : ((kMmaK * TC_ROW_BYTES) >> 4);
+            constexpr uint64_t kBDescK = (kMmaK * TC_ROW_BYTES) >> 4;
             int acc = 0;
             uint32_t acc_phase = 0;
             bool ok = true;

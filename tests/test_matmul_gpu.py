@@ -320,7 +320,8 @@ def test_tf32_rounds_halfway_to_even(native, rows):
     """Bit-exact known answers: reference test_matmul.py:101-111 and test_triton_matmul.py:45-53.
 
     One row runs on the small-problem FFMA path (K tiles rounded in shared memory),
-    4096 rows x 1024 columns on the tensor cores (operands rounded by the pre-pass)."""
+    4096 rows x 1024 columns on the tensor cores (operands rounded by the TMA loads of
+    their TFLOAT32 tensor maps)."""
     bits = np.array([0x3f801000, 0x3f803000, 0x3f800fff, 0x3f801001,
                      0xbf801000, 0xbf803000, 0xbf800fff, 0xbf801001], dtype=np.uint32)
     values = np.tile(bits.view(np.float32).reshape(1, -1), (rows, 1 if rows == 1 else 128))

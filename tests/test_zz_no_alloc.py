@@ -3,14 +3,13 @@
 Some callers cannot allocate device memory at call time: their framework has
 already reserved nearly all of it in its own pool, and one more allocation
 would fail or force the pool to give memory back.  For them the library has a second launch
-entry point whose scratch (TF32-rounded and repacked operand copies) lives in
+entry point whose scratch (repacked copies of unaligned operands) lives in
 a fixed 32 MiB array compiled into the library.  These tests call it through
 the C-ABI and check that, on two calls in a row, it gives the same output as
 matmul_launch (within the tolerance used by every other parity test here, and
-against the FP64 oracle) on every kind of scratch use: TF32 rounding copies for
-the single-CTA and skinny kernels, and repacked unaligned FP16/BF16 operands,
-split K included; and that a problem too large for the array is rejected with a
-clear error.  The file name makes pytest collect it last.
+against the FP64 oracle) on every kind of scratch use: repacked unaligned TF32,
+FP16 and BF16 operands for the single-CTA, split-K and skinny kernels; and that a
+problem too large for the array is rejected with a clear error.  The file name makes pytest collect it last.
 """
 
 from __future__ import annotations
@@ -62,14 +61,15 @@ def _launch(fn, native, precision, a, b, out):
     return rc, err.value.decode()
 
 
-# TF32 problems above m*k*n = 2^25 run on the tensor cores and place their rounded
-# copies of A and B^T in the fixed array; smaller ones run on the FFMA kernel and
-# need no scratch, so every TF32 case here is above that size.
+# Only operands TMA cannot address (base not 16-byte aligned, or a row pitch that
+# is not a multiple of 16 bytes) are copied into scratch; TF32 problems up to
+# m*k*n = 2^25 run on the FFMA kernel and need none, so every TF32 case here is
+# larger than that and has an unaligned operand.
 @pytest.mark.parametrize("precision,shape,offset", [
-    ("tf32", (384, 260, 516), False),     # scratch: rounded A and transposed B (single-CTA tiles)
-    ("tf32", (257, 300, 515), True),      # scratch: the same from unaligned operands
-    ("tf32", (512, 1024, 512), False),    # scratch: 4 MiB of rounded copies
-    ("tf32", (48, 1024, 1024), False),    # scratch: rounded copies feeding the skinny (m <= 64) kernel
+    ("tf32", (384, 260, 517), False),     # scratch: repacked B (n % 4 != 0; single-CTA tiles)
+    ("tf32", (257, 300, 515), True),      # scratch: repacked A and B (offset bases)
+    ("tf32", (512, 1026, 512), False),    # scratch: repacked A (k % 4 != 0), 2 MiB
+    ("tf32", (48, 1024, 1022), False),    # scratch: repacked B feeding the skinny (m <= 64) kernel
     ("bf16", (513, 129, 577), True),      # scratch: repacked unaligned operands
     ("bf16", (130, 4099, 258), True),     # scratch: repacked operands of a split-K launch
     ("fp16", (256, 512, 512), False),     # aligned: no scratch needed
@@ -98,7 +98,7 @@ def test_noalloc_matches_matmul_launch_on_two_calls(native, precision, shape, of
 def test_noalloc_rejects_problems_beyond_the_fixed_array(native):
     lib = native.library
     _bind(lib)
-    m = k = n = 4096                      # TF32 copies need 128 MiB > 32 MiB
+    m, k, n = 4096, 4096, 4097            # repacked TF32 B (n % 4 != 0) needs 64 MiB > 32 MiB
     a = torch.zeros((m, k), dtype=torch.float32, device="cuda")
     b = torch.zeros((k, n), dtype=torch.float32, device="cuda")
     out = torch.zeros((m, n), dtype=torch.float32, device="cuda")
