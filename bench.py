@@ -510,8 +510,8 @@ def multi_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
 
         c = symm_mem.empty((m, n), dtype=torch.float32, device=device)
         handle = symm_mem.rendezvous(c, dist.group.WORLD)
-        gather_all = CopyEngineGather(plan, c, handle=handle)
-        gather_root = CopyEngineGather(plan_root, c, handle=handle)
+        gather_all = CopyEngineGather(plan, c, handle=handle, streams=args.ce_streams)
+        gather_root = CopyEngineGather(plan_root, c, handle=handle, streams=args.ce_streams)
     else:
         c = torch.empty((m, n), dtype=torch.float32, device=device)
     dist.broadcast(b, src=0)                            # the first step's B, before the loop
@@ -664,7 +664,8 @@ def multi_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
                                   f"all-gathers C in {plan.chunk_count} row chunks, each chunk's exchange "
                                   f"overlapping the next chunk's GEMM",
                    "exchange": ("copy-engine pushes into the peers' C (symmetric memory, one cudaMemcpyAsync "
-                                "per peer and chunk), completed by a one-element NCCL all-reduce")
+                                f"per peer and chunk, peers rank+1, rank+2, ... on {args.ce_streams} copy "
+                                "stream(s)), completed by a one-element NCCL all-reduce")
                    if use_ce else "grouped NCCL send/recv of each chunk",
                    "chunks": plan.chunk_count, "gemm_sms": gemm_sms, "l2": "inputs larger than L2"},
         "t1": {"ms": t1_ms, "tflops": t1_value, "fastest_gpu_ms": float(t1_min.item()),
@@ -700,6 +701,8 @@ def main() -> int:
                         help="multi-GPU: SMs left free of GEMM CTAs for the NCCL kernels that overlap them")
     parser.add_argument("--exchange", choices=("ce", "nccl"), default="ce",
                         help="multi-GPU C exchange: copy-engine pushes over symmetric memory, or NCCL send/recv")
+    parser.add_argument("--ce-streams", type=int, default=1,
+                        help="copy streams of the copy-engine exchange (peers visited rank+1, rank+2, ...)")
     parser.add_argument("--quick", action="store_true", help="skip the per-precision and cuBLAS tables")
     parser.add_argument("--sweep", choices=("square", "llm", "ragged", "all", "legacy"), default=None,
                         help="instead of the contract line, time every shape of a configuration "

@@ -201,10 +201,17 @@ class CopyEngineGather:
     chunk's GEMM) has completed; ``finish()`` makes the current stream wait for
     this rank's pushes and runs a one-element all-reduce that completes only when
     every rank's pushes are done.  Every rank calls ``finish()`` once per step.
+
+    The receivers are visited in the order rank + 1, rank + 2, ... (mod world)
+    and spread round-robin over ``streams`` copy streams: with one stream each
+    rank sends to one peer at a time and, since every rank walks the same
+    offsets, each rank also receives from about one peer at a time.  Copies to
+    all peers at once (one stream per peer) measured about 400 GB/s of ingress
+    per GPU at 8 GPUs, against 733 GB/s for a single peer-to-peer flow.
     """
 
     def __init__(self, plan: ShardPlan, c_full: torch.Tensor, group=None, handle=None, *, copy=None,
-                 new_stream=None):
+                 new_stream=None, streams: int = 1):
         self.plan = plan
         self.c_full = c_full
         self.group = group if group is not None else dist.group.WORLD
@@ -217,8 +224,12 @@ class CopyEngineGather:
         if new_stream is None:
             new_stream = lambda: torch.cuda.Stream(device=c_full.device)  # noqa: E731
         shape, dtype = tuple(c_full.shape), c_full.dtype
-        self.peer_c = {peer: self.handle.get_buffer(peer, shape, dtype) for peer in plan.receivers()}
-        self.streams = {peer: new_stream() for peer in plan.receivers()}
+        world, rank = plan.world, plan.rank
+        receivers = set(plan.receivers())
+        self.order = [(rank + d) % world for d in range(1, world) if (rank + d) % world in receivers]
+        self.peer_c = {peer: self.handle.get_buffer(peer, shape, dtype) for peer in self.order}
+        count = max(1, min(streams, len(self.order))) if self.order else 0
+        self.streams = [new_stream() for _ in range(count)]
         self.token = torch.zeros(1, dtype=torch.float32, device=c_full.device)
         self.row_bytes = c_full.shape[1] * c_full.element_size()
 
@@ -227,13 +238,15 @@ class CopyEngineGather:
         if hi <= lo:
             return
         src = self.c_full.data_ptr() + lo * self.row_bytes
-        for peer, stream in self.streams.items():
+        for stream in self.streams:
             stream.wait_event(event)
-            self.copy(self.peer_c[peer].data_ptr() + lo * self.row_bytes, src, (hi - lo) * self.row_bytes, stream)
+        for i, peer in enumerate(self.order):
+            self.copy(self.peer_c[peer].data_ptr() + lo * self.row_bytes, src, (hi - lo) * self.row_bytes,
+                      self.streams[i % len(self.streams)])
 
     def finish(self) -> None:
         current = torch.cuda.current_stream(self.c_full.device)
-        for stream in self.streams.values():
+        for stream in self.streams:
             current.wait_stream(stream)
         dist.all_reduce(self.token, group=self.group)
 

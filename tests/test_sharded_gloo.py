@@ -172,9 +172,10 @@ def _memmove_copy(dst, src, nbytes, stream):
     ctypes.memmove(dst, src, nbytes)
 
 
+@pytest.mark.parametrize("streams", (1, 3))
 @pytest.mark.parametrize("world,m,chunks,gather", [(2, 37, 3, "all"), (3, 64, 4, "all"), (4, 9, 8, "all"),
                                                    (3, 50, 2, "root"), (8, 100, 3, "all")])
-def test_copy_engine_gather_places_every_chunk(world, m, chunks, gather):
+def test_copy_engine_gather_places_every_chunk(world, m, chunks, gather, streams):
     """CopyEngineGather's row arithmetic: after every rank has posted every chunk,
     each receiver's C holds every sender's rows at the right place (all ranks in one
     process, host buffers standing in for the peers' mapped C, memmove for the copy)."""
@@ -191,7 +192,11 @@ def test_copy_engine_gather_places_every_chunk(world, m, chunks, gather):
         buffers.append(c)
     handle = _FakeHandle(buffers)
     gathers = [CopyEngineGather(plan, buffers[r], group=object(), handle=handle, copy=_memmove_copy,
-                                new_stream=_FakeStream) for r, plan in enumerate(plans)]
+                                new_stream=_FakeStream, streams=streams) for r, plan in enumerate(plans)]
+    for r, g in enumerate(gathers):
+        # Peers in the order rank+1, rank+2, ... so that every rank sends to a different peer at a time.
+        assert g.order == [p for p in ((r + d) % world for d in range(1, world)) if p in plans[r].receivers()]
+        assert len(g.streams) == (min(streams, len(g.order)) if g.order else 0)
     for index in range(plans[0].chunk_count):
         for g in gathers:
             g.post(index, event=None)
