@@ -473,7 +473,8 @@ def multi_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
     import torch.distributed as dist
 
     from gpumat import NativeMatmul
-    from sharded import BroadcastPipeline, CopyEngineGather, ShardPlan, pipelined_step, pipelined_step_ce
+    from sharded import (BroadcastPipeline, CopyEngineGather, KernelPushGather, ShardPlan, pipelined_step,
+                         pipelined_step_ce)
 
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
@@ -504,14 +505,21 @@ def multi_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
         b32 = torch.rand((k, n), generator=gen, device=device) * 2 - 1
         native.convert(b32, b, "bf16")
         del b32
-    use_ce = args.exchange == "ce"
+    use_ce = args.exchange in ("ce", "push")
     if use_ce:
         import torch.distributed._symmetric_memory as symm_mem
 
         c = symm_mem.empty((m, n), dtype=torch.float32, device=device)
         handle = symm_mem.rendezvous(c, dist.group.WORLD)
-        gather_all = CopyEngineGather(plan, c, handle=handle, streams=args.ce_streams)
-        gather_root = CopyEngineGather(plan_root, c, handle=handle, streams=args.ce_streams)
+        if args.exchange == "ce":
+            gather_all = CopyEngineGather(plan, c, handle=handle, streams=args.ce_streams)
+            gather_root = CopyEngineGather(plan_root, c, handle=handle, streams=args.ce_streams)
+        else:
+            def push(src, dsts, nbytes, push_stream, ctas):
+                native.peer_push(src, dsts, nbytes, stream=push_stream, ctas=ctas)
+
+            gather_all = KernelPushGather(plan, c, push, handle=handle, ctas=args.push_ctas)
+            gather_root = KernelPushGather(plan_root, c, push, handle=handle, ctas=args.push_ctas)
     else:
         c = torch.empty((m, n), dtype=torch.float32, device=device)
     dist.broadcast(b, src=0)                            # the first step's B, before the loop
@@ -666,7 +674,11 @@ def multi_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
                    "exchange": ("copy-engine pushes into the peers' C (symmetric memory, one cudaMemcpyAsync "
                                 f"per peer and chunk, peers rank+1, rank+2, ... on {args.ce_streams} copy "
                                 "stream(s)), completed by a one-element NCCL all-reduce")
-                   if use_ce else "grouped NCCL send/recv of each chunk",
+                   if args.exchange == "ce" else
+                   (f"this library's push kernel (matmul_peer_push, {args.push_ctas or 16} CTAs on the SMs the "
+                    "GEMM leaves free) storing each chunk into every peer's C over NVLink, completed by a "
+                    "one-element NCCL all-reduce") if args.exchange == "push"
+                   else "grouped NCCL send/recv of each chunk",
                    "chunks": plan.chunk_count, "gemm_sms": gemm_sms, "l2": "inputs larger than L2"},
         "t1": {"ms": t1_ms, "tflops": t1_value, "fastest_gpu_ms": float(t1_min.item()),
                "how": "the whole problem as one GEMM on each GPU at once, in the same run (max over GPUs)",
@@ -699,8 +711,10 @@ def main() -> int:
     parser.add_argument("--chunks", type=int, default=8)
     parser.add_argument("--reserve-sms", type=int, default=16,
                         help="multi-GPU: SMs left free of GEMM CTAs for the NCCL kernels that overlap them")
-    parser.add_argument("--exchange", choices=("ce", "nccl"), default="ce",
-                        help="multi-GPU C exchange: copy-engine pushes over symmetric memory, or NCCL send/recv")
+    parser.add_argument("--exchange", choices=("ce", "push", "nccl"), default="ce",
+                        help="multi-GPU C exchange: copy-engine pushes over symmetric memory, this library's "
+                             "push kernel over symmetric memory, or NCCL send/recv")
+    parser.add_argument("--push-ctas", type=int, default=16, help="CTAs of the push kernel (--exchange push)")
     parser.add_argument("--ce-streams", type=int, default=1,
                         help="copy streams of the copy-engine exchange (peers visited rank+1, rank+2, ...)")
     parser.add_argument("--quick", action="store_true", help="skip the per-precision and cuBLAS tables")

@@ -129,6 +129,19 @@ int matmul_set_sm_limit(void *context, int sms, char *error, size_t error_size);
  * forms have no waits. */
 int matmul_set_wait_limit(void *context, unsigned long long nanoseconds, char *error, size_t error_size);
 
+/* No counterpart in the reference (which runs on one GPU).  Copies `bytes` (a
+ * multiple of 16) from `src` on this context's device into each of the `peers`
+ * (at most 7) device addresses `peer_dst[0..peers-1]` -- the same block in other
+ * GPUs' buffers mapped into this process (peer-enabled allocations, e.g. symmetric
+ * memory) -- with 16-byte loads of this GPU's memory and 16-byte stores over
+ * NVLink, on `ctas` CTAs (0 = 16) of `stream`, asynchronously.  The C exchange of
+ * the row-sharded multi-GPU GEMM: each finished row block of C goes to every
+ * peer while the next block's GEMM runs on the remaining SMs.  All pointers must
+ * be 16-byte aligned.  Completion on the peers is the caller's to order (a
+ * collective after this launch on every rank). */
+int matmul_peer_push(void *context, const void *src, void *const *peer_dst, int peers, size_t bytes, int ctas,
+                     void *stream, char *error, size_t error_size);
+
 /* No counterpart in the reference.  Same arguments, result and error convention
  * as matmul_launch, for implementation 7 (tcgen05) only, but it never allocates:
  * for callers that must not call cudaMalloc or a stream-ordered allocator --

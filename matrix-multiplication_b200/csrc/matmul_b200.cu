@@ -23,6 +23,7 @@
 #include "tc2_gemm.cuh"
 #include "tc_skinny.cuh"
 #include "check.cuh"
+#include "peer_push.cuh"
 #include <cmath>
 
 // Scratch for matmul_launch_noalloc: a fixed array in the module's device
@@ -1176,6 +1177,44 @@ extern "C" int matmul_set_wait_limit(void *opaque, unsigned long long nanosecond
     if (nanoseconds > kWaitLimitNs)
         return fail(error, error_size, "matmul_set_wait_limit", "the limit cannot exceed 2 s (2000000000 ns)");
     static_cast<Context *>(opaque)->wait_limit_ns = nanoseconds;
+    return 0;
+}
+
+extern "C" int matmul_peer_push(void *opaque, const void *src, void *const *peer_dst, int peers, size_t bytes,
+                                int ctas, void *stream, char *error, size_t error_size)
+{
+    clear_error(error, error_size);
+    if (!opaque)
+        return fail(error, error_size, "matmul_peer_push", "context is null");
+    if (peers < 0 || peers > PP_MAX_PEERS)
+        return fail(error, error_size, "matmul_peer_push", "peers must be between 0 and 7");
+    if (bytes % 16 != 0)
+        return fail(error, error_size, "matmul_peer_push", "the block size must be a multiple of 16 bytes");
+    if (ctas < 0)
+        return fail(error, error_size, "matmul_peer_push", "ctas must be 0 (the default) or positive");
+    if (peers == 0 || bytes == 0)
+        return 0;
+    if (!src || !peer_dst || !aligned16(src))
+        return fail(error, error_size, "matmul_peer_push", "source is null or not 16-byte aligned");
+    PeerPushJob job{};
+    job.src = static_cast<const float4 *>(src);
+    job.peers = peers;
+    job.count = static_cast<long long>(bytes / 16);
+    for (int p = 0; p < peers; ++p) {
+        if (!peer_dst[p] || !aligned16(peer_dst[p]))
+            return fail(error, error_size, "matmul_peer_push", "a destination is null or not 16-byte aligned");
+        job.dst[p] = static_cast<float4 *>(peer_dst[p]);
+    }
+    Context *ctx = static_cast<Context *>(opaque);
+    cudaError_t st = cudaSetDevice(ctx->device);
+    if (st != cudaSuccess)
+        return fail_cuda(error, error_size, "cudaSetDevice", st);
+    const long long needed = (job.count + PP_THREADS - 1) / PP_THREADS;
+    const int grid = static_cast<int>(needed < (ctas ? ctas : 16) ? needed : (ctas ? ctas : 16));
+    peer_push_kernel<<<grid, PP_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(job);
+    st = cudaGetLastError();
+    if (st != cudaSuccess)
+        return fail(error, error_size, "matmul_peer_push", cudaGetErrorString(st));
     return 0;
 }
 

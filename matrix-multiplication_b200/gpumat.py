@@ -72,6 +72,7 @@ EXPORTS: dict[str, tuple[tuple, object, bool]] = {
     "matmul_plan": ((_P, _I, _I, _I, _I, _I, ctypes.c_char_p, ctypes.c_size_t), ctypes.c_int, True),
     "matmul_set_sm_limit": ((_P, _I), ctypes.c_int, True),
     "matmul_set_wait_limit": ((_P, ctypes.c_ulonglong), ctypes.c_int, True),
+    "matmul_peer_push": ((_P, _P, ctypes.POINTER(_P), _I, ctypes.c_size_t, _I, _P), ctypes.c_int, True),
 }
 
 
@@ -320,6 +321,15 @@ class NativeMatmul:
         self._lib.invoke("matmul_check_fp64", handle, PRECISION_IDS[precision], _P(a.data_ptr()),
                          _P(b.data_ptr()), _P(out.data_ptr()), m, k, n, _P(stream.cuda_stream), result)
         return float(result[0]), float(result[1])
+
+    def peer_push(self, src_ptr: int, peer_ptrs: list[int], nbytes: int, stream=None, ctas: int = 0) -> None:
+        """Copy ``nbytes`` at device address ``src_ptr`` into each address of
+        ``peer_ptrs`` (peers' mapped buffers) on ``stream`` (default: current)."""
+        handle = self.handle
+        stream = stream if stream is not None else torch.cuda.current_stream(self._device)
+        dsts = (_P * max(1, len(peer_ptrs)))(*[_P(p) for p in peer_ptrs])
+        self._lib.invoke("matmul_peer_push", handle, _P(src_ptr), dsts, len(peer_ptrs), nbytes, ctas,
+                         _P(stream.cuda_stream))
 
     def device_status(self, clear: bool = True) -> int:
         """Synchronize and return the device status word (0 = no kernel's wait ran out)."""

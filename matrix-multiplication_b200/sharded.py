@@ -251,9 +251,10 @@ class CopyEngineGather:
         dist.all_reduce(self.token, group=self.group)
 
 
-def pipelined_step_ce(plan: ShardPlan, a_local: torch.Tensor, pipe: BroadcastPipeline, gather: CopyEngineGather,
+def pipelined_step_ce(plan: ShardPlan, a_local: torch.Tensor, pipe: BroadcastPipeline, gather,
                       gemm: Callable[[torch.Tensor, torch.Tensor, torch.Tensor], None]) -> None:
-    """``pipelined_step`` with the C exchange on copy engines (``CopyEngineGather``)."""
+    """``pipelined_step`` with the C exchange of ``gather`` (``CopyEngineGather`` or
+    ``KernelPushGather``): each chunk is posted as soon as its GEMM is enqueued."""
     if plan.world > 1:
         pipe.start()
     start, _ = plan.local_rows
@@ -267,3 +268,51 @@ def pipelined_step_ce(plan: ShardPlan, a_local: torch.Tensor, pipe: BroadcastPip
     if plan.world > 1:
         gather.finish()
         pipe.finish()
+
+
+class KernelPushGather:
+    """C exchange of a row-sharded GEMM by this library's push kernel (``matmul_peer_push``).
+
+    The same contract as ``CopyEngineGather``: ``c_full`` comes from
+    ``torch.distributed._symmetric_memory.empty`` on every rank; ``post(index,
+    event)`` sends chunk ``index`` to every receiver once ``event`` has completed,
+    here as one kernel launch on a side stream that stores the rows into all the
+    receivers' C over NVLink; ``finish()`` joins the side stream and runs the
+    one-element all-reduce that completes when every rank's pushes are done.  The
+    kernel runs on SMs the GEMM leaves free (``matmul_set_sm_limit``).
+    """
+
+    def __init__(self, plan: ShardPlan, c_full: torch.Tensor, push, group=None, handle=None, *, ctas: int = 0,
+                 new_stream=None):
+        self.plan = plan
+        self.c_full = c_full
+        self.push = push            # push(src_ptr, [dst_ptr, ...], nbytes, stream, ctas)
+        self.ctas = ctas
+        self.group = group if group is not None else dist.group.WORLD
+        if handle is None:
+            import torch.distributed._symmetric_memory as symm_mem
+
+            handle = symm_mem.rendezvous(c_full, self.group)
+        self.handle = handle
+        world, rank = plan.world, plan.rank
+        receivers = set(plan.receivers())
+        self.order = [(rank + d) % world for d in range(1, world) if (rank + d) % world in receivers]
+        # Each peer's C as this process sees it (the same view CopyEngineGather copies into).
+        shape, dtype = tuple(c_full.shape), c_full.dtype
+        self.peer_base = {peer: self.handle.get_buffer(peer, shape, dtype).data_ptr() for peer in self.order}
+        self.stream = (new_stream or (lambda: torch.cuda.Stream(device=c_full.device)))()
+        self.token = torch.zeros(1, dtype=torch.float32, device=c_full.device)
+        self.row_bytes = c_full.shape[1] * c_full.element_size()
+
+    def post(self, index: int, event) -> None:
+        lo, hi = self.plan.global_chunk(self.plan.rank, index)
+        if hi <= lo or not self.order:
+            return
+        self.stream.wait_event(event)
+        byte_offset = lo * self.row_bytes
+        self.push(self.c_full.data_ptr() + byte_offset, [self.peer_base[p] + byte_offset for p in self.order],
+                  (hi - lo) * self.row_bytes, self.stream, self.ctas)
+
+    def finish(self) -> None:
+        torch.cuda.current_stream(self.c_full.device).wait_stream(self.stream)
+        dist.all_reduce(self.token, group=self.group)

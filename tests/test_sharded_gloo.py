@@ -209,3 +209,41 @@ def test_copy_engine_gather_places_every_chunk(world, m, chunks, gather, streams
             outside = torch.ones(m, dtype=torch.bool)
             outside[lo:hi] = False
             assert torch.all(buffers[r][outside] == -1.0)
+
+
+@pytest.mark.parametrize("world,m,chunks,gather", [(2, 37, 3, "all"), (4, 9, 8, "all"), (3, 50, 2, "root"),
+                                                   (8, 100, 3, "all")])
+def test_kernel_push_gather_places_every_chunk(world, m, chunks, gather):
+    """KernelPushGather's addresses: each post hands the push function this rank's
+    chunk and the matching rows of every receiver's C (memmove standing in for the
+    push kernel, all ranks in one process)."""
+    import ctypes
+
+    from sharded import KernelPushGather
+
+    n = 6
+    expected = torch.arange(m * n, dtype=torch.float32).reshape(m, n)
+    plans = [ShardPlan(m, 3, n, world, r, chunks=chunks, gather=gather) for r in range(world)]
+    buffers = []
+    for plan in plans:
+        c = torch.full((m, n), -1.0)
+        lo, hi = plan.local_rows
+        c[lo:hi] = expected[lo:hi]
+        buffers.append(c)
+    handle = _FakeHandle(buffers)
+    calls = []
+
+    def push(src, dsts, nbytes, stream, ctas):
+        calls.append(len(dsts))
+        for dst in dsts:
+            ctypes.memmove(dst, src, nbytes)
+
+    gathers = [KernelPushGather(plan, buffers[r], push, group=object(), handle=handle, new_stream=_FakeStream)
+               for r, plan in enumerate(plans)]
+    for index in range(plans[0].chunk_count):
+        for g in gathers:
+            g.post(index, event=None)
+    for r in range(world):
+        if gather == "all" or r == 0:
+            assert torch.equal(buffers[r], expected), r
+    assert max(calls) == (world - 1 if gather == "all" else 1)
