@@ -556,19 +556,20 @@ def multi_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
         pipe.start()
         pipe.finish()
 
-    def exchange_only():
+    def exchange_only(root: bool = False):
         if use_ce:
+            gather = gather_root if root else gather_all
             for index in range(plan.chunk_count):
                 event = torch.cuda.Event()
                 event.record()
-                gather_all.post(index, event)
-            gather_all.finish()
+                gather.post(index, event)
+            gather.finish()
         else:
             from sharded import exchange_chunk
 
             works = []
             for index in range(plan.chunk_count):
-                works.extend(exchange_chunk(plan, index, c))
+                works.extend(exchange_chunk(plan_root if root else plan, index, c))
             for work in works:
                 work.wait()
 
@@ -590,27 +591,42 @@ def multi_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
         return float(ms.item()), (wall0, wall1)
 
+    step_main, step_other = (step_root, step_all) if args.gather == "root" else (step_all, step_root)
     with ClockSampler(local_rank) as clocks:
-        ms_per_step, window = timed(step_all, args.steps, args.warmup)
+        ms_per_step, window = timed(step_main, args.steps, args.warmup)
     clock_summary = clocks.summary(*window)
     side_steps = max(3, min(args.steps, 10))
     breakdown = {
-        "gather_to_rank0_ms": timed(step_root, side_steps, 2)[0],
+        ("all_gather_ms" if args.gather == "root" else "gather_to_rank0_ms"): timed(step_other, side_steps, 2)[0],
         "gemm_only_ms": timed(gemm_only, side_steps, 2)[0],
         "broadcast_only_ms": timed(broadcast_only, side_steps, 2)[0],
         "exchange_only_ms": timed(exchange_only, side_steps, 2)[0],
+        "exchange_to_rank0_only_ms": timed(lambda: exchange_only(root=True), side_steps, 2)[0],
     }
 
-    # FP64 check of rows this rank received from the next rank (its A shard is
-    # regenerated here from the same seed): the GEMM and the exchange together.
+    # FP64 check of rows received from a peer (its A shard is regenerated here
+    # from the same seed): the GEMM and the exchange together.  All-gather: each
+    # rank checks 64 rows of the next rank's shard; gather to root: rank 0 checks
+    # 64 rows of every other rank's shard.
+    def check_rows(owners) -> list[float]:
+        worst = [0.0, 0.0]
+        for owner in owners:
+            owner_lo = plan.rows[owner][0]
+            band = min(64, plan.rows[owner][1] - owner_lo)
+            a_owner = shard_a(owner)
+            ratio, max_err = native.check_fp64(a_owner[:band], pipe.current, c[owner_lo:owner_lo + band], "bf16")
+            del a_owner
+            worst = [max(worst[0], ratio), max(worst[1], max_err)]
+        return worst
+
+    c.fill_(float("nan"))
     timed(step_all, 1, 0)
-    owner = (rank + 1) % world
-    owner_lo = plan.rows[owner][0]
-    band = min(64, plan.rows[owner][1] - owner_lo)
-    a_owner = shard_a(owner)
-    ratio, max_err = native.check_fp64(a_owner[:band], pipe.current, c[owner_lo:owner_lo + band], "bf16")
-    del a_owner
-    check = torch.tensor([ratio, max_err], device=device, dtype=torch.float64)
+    check = torch.tensor(check_rows([(rank + 1) % world]), device=device, dtype=torch.float64)
+    c.fill_(float("nan"))
+    timed(step_root, 1, 0)
+    root_check = torch.tensor(check_rows(range(1, world)) if rank == 0 else [0.0, 0.0], device=device,
+                              dtype=torch.float64)
+    check = torch.maximum(check, root_check)
     dist.all_reduce(check, op=dist.ReduceOp.MAX)
 
     # T1: the whole problem on one GPU, measured on every GPU at once (no SM limit).
@@ -628,10 +644,12 @@ def multi_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
     native.set_sm_limit(gemm_sms if gemm_sms < sms else 0)
 
     # End to end: pinned FP32 host A shard (every rank) and B (rank 0) -> device,
-    # RNE conversion, the sharded step, this rank's C rows back to pinned host memory.
+    # RNE conversion, the sharded step, the step's result back to pinned host
+    # memory (gather to root: the whole C from rank 0; all-gather: each rank's rows).
     host_a = (torch.rand((stop - start, k), device=device) * 2 - 1).cpu().pin_memory()
     host_b = (torch.rand((k, n), device=device) * 2 - 1).cpu().pin_memory() if rank == 0 else None
-    host_c = torch.empty((stop - start, n), dtype=torch.float32).pin_memory()
+    c_result = (c if rank == 0 else None) if args.gather == "root" else c[start:stop]
+    host_c = torch.empty(c_result.shape, dtype=torch.float32).pin_memory() if c_result is not None else None
     dev_a32 = torch.empty((stop - start, k), dtype=torch.float32, device=device)
     dev_b32 = torch.empty((k, n), dtype=torch.float32, device=device) if rank == 0 else None
 
@@ -641,13 +659,14 @@ def multi_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
         if rank == 0:
             dev_b32.copy_(host_b, non_blocking=True)
             native.convert(dev_b32, pipe.pending, "bf16")
-        step_all()
-        host_c.copy_(c[start:stop], non_blocking=True)
+        step_main()
+        if host_c is not None:
+            host_c.copy_(c_result, non_blocking=True)
 
     e2e_ms, _ = timed(e2e_step, 3, 1)
     h2d = (stop - start) * k * 4 + (k * n * 4 if rank == 0 else 0)
-    d2h = (stop - start) * n * 4
-    del host_a, host_b, host_c, dev_a32, dev_b32
+    d2h = c_result.numel() * 4 if c_result is not None else 0
+    del host_a, host_b, host_c, c_result, dev_a32, dev_b32
 
     status = native.device_status()
     status_t = torch.tensor([status], device=device, dtype=torch.int64)
@@ -669,8 +688,10 @@ def multi_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
         "config": {"workload": f"rowshard_bf16_{m}x{k}x{n}", "m": m, "k": k, "n": n, "precision": "bf16",
                    "parallelism": f"row-sharded A/C over {world} ranks; every step broadcasts one B (NCCL, own "
                                   f"communicator, posted one step ahead and overlapping the GEMMs) and "
-                                  f"all-gathers C in {plan.chunk_count} row chunks, each chunk's exchange "
-                                  f"overlapping the next chunk's GEMM",
+                                  + ("gathers C on rank 0" if args.gather == "root" else "all-gathers C")
+                                  + f" in {plan.chunk_count} row chunks, each chunk's exchange overlapping the "
+                                  f"next chunk's GEMM",
+                   "gather": args.gather,
                    "exchange": ("copy-engine pushes into the peers' C (symmetric memory, one cudaMemcpyAsync "
                                 f"per peer and chunk, peers rank+1, rank+2, ... on {args.ce_streams} copy "
                                 "stream(s)), completed by a one-element NCCL all-reduce")
@@ -691,9 +712,12 @@ def multi_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
         "e2e": {"value": tflops(m, k, n, e2e_ms), "unit": "TFLOP/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "path": "pinned FP32 host A shard (every rank) and B (rank 0) -> H2D -> matmul_convert (RNE) -> "
-                        "sharded step -> D2H of this rank's C rows; rank 0's numbers (max over ranks of time)"},
+                        "sharded step -> D2H of the result (gather to root: the whole C from rank 0; all-gather: "
+                        "each rank's own rows); byte counts are rank 0's, time the max over ranks"},
         "check": {"check_fp64_ratio_max": float(check[0].item()), "check_fp64_max_abs_err": float(check[1].item()),
-                  "what": "64 rows of the next rank's shard as received by each rank, against an FP64 product"},
+                  "what": "after an all-gather step, 64 rows of the next rank's shard as received by each rank; "
+                          "after a gather-to-root step, 64 rows of every other rank's shard on rank 0; "
+                          "against an FP64 product (C filled with NaN before each step)"},
         "gpu_launches": args.steps * plan.chunk_count,
         "clocks": clock_summary, "device_status": int(status_t.item()),
     }
@@ -715,6 +739,10 @@ def main() -> int:
                         help="multi-GPU C exchange: copy-engine pushes over symmetric memory, this library's "
                              "push kernel over symmetric memory, or NCCL send/recv")
     parser.add_argument("--push-ctas", type=int, default=16, help="CTAs of the push kernel (--exchange push)")
+    parser.add_argument("--gather", choices=("root", "all"), default="all",
+                        help="multi-GPU: where C is assembled in the timed step -- on rank 0 (the single-GPU "
+                             "call's result, on one device) or on every rank; the other variant is timed "
+                             "in the same run")
     parser.add_argument("--ce-streams", type=int, default=1,
                         help="copy streams of the copy-engine exchange (peers visited rank+1, rank+2, ...)")
     parser.add_argument("--quick", action="store_true", help="skip the per-precision and cuBLAS tables")
