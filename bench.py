@@ -18,10 +18,12 @@ Metric: device-timed TFLOP/s = 2*M*K*N / t (the reference's src/main.py:102).
   end-to-end figure through the public API with host buffers.
 * N > 1 (default workload ``rowshard32768``): M=K=N=32768 BF16, U[-1,1), A and C
   row-sharded over the ranks; every step broadcasts one B from rank 0 (posted
-  one step ahead on its own communicator, overlapping the GEMMs) and
-  all-gathers C in row chunks that overlap the next chunk's GEMM, with
-  ``--reserve-sms`` SMs left to the NCCL kernels; one process per GPU under
-  torchrun; time = max over ranks.
+  one step ahead on its own communicator, overlapping the GEMMs) and gathers C
+  on rank 0 (``--gather root``, the default: the single-GPU call's result, on
+  one device) or on every rank (``--gather all``) in row chunks that overlap
+  the next chunk's GEMM, with ``--reserve-sms`` SMs left to the NCCL kernels;
+  one process per GPU under torchrun; time = max over ranks.  The other gather
+  variant, each part of a step alone and T1 are timed in the same run.
 * ``--impl reference`` times the reference's CPU path (numpy FP32 GEMM,
   src/benchmark_backends.py:223-226) on the host cores over row slabs of the
   same workload; under torchrun only rank 0 runs it.
@@ -458,14 +460,15 @@ def multi_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
     """Row-sharded 32768^3 BF16 GEMM over `world` ranks (one process per GPU).
 
     A step: broadcast of the next step's B (NCCL, own communicator, one step
-    ahead), the local rows' GEMMs in row chunks, and the C all-gather of every
-    chunk as soon as it is done -- by copy-engine pushes into the peers' C
-    (``--exchange ce``, no SM taken from the GEMM) or by grouped NCCL send/recv
-    (``--exchange nccl``).  Time per step = max over ranks of CUDA-event time.
-    The same run also measures, on every rank: the gather-to-rank-0 variant,
-    each part of a step alone (GEMMs, broadcast, exchange), T1 (the whole
-    problem on one GPU, all GPUs at once), an FP64 check of rows received from
-    a peer, and an end-to-end step from pinned FP32 host buffers.
+    ahead), the local rows' GEMMs in row chunks, and the C gather of every chunk
+    as soon as it is done, to rank 0 (``--gather root``) or to every rank
+    (``--gather all``) -- by copy-engine pushes into the peers' C (``--exchange
+    ce``, no SM taken from the GEMM), by this library's push kernel (``push``) or
+    by grouped NCCL send/recv (``nccl``).  Time per step = max over ranks of
+    CUDA-event time.  The same run also measures, on every rank: the other
+    gather variant, each part of a step alone (GEMMs, broadcast, exchange), T1
+    (the whole problem on one GPU, all GPUs at once), an FP64 check of rows
+    received from peers, and an end-to-end step from pinned FP32 host buffers.
     """
     import datetime
 
@@ -739,7 +742,7 @@ def main() -> int:
                         help="multi-GPU C exchange: copy-engine pushes over symmetric memory, this library's "
                              "push kernel over symmetric memory, or NCCL send/recv")
     parser.add_argument("--push-ctas", type=int, default=16, help="CTAs of the push kernel (--exchange push)")
-    parser.add_argument("--gather", choices=("root", "all"), default="all",
+    parser.add_argument("--gather", choices=("root", "all"), default="root",
                         help="multi-GPU: where C is assembled in the timed step -- on rank 0 (the single-GPU "
                              "call's result, on one device) or on every rank; the other variant is timed "
                              "in the same run")
