@@ -599,13 +599,36 @@ def multi_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
         ms_per_step, window = timed(step_main, args.steps, args.warmup)
     clock_summary = clocks.summary(*window)
     side_steps = max(3, min(args.steps, 10))
-    breakdown = {
+    breakdown = {} if args.quick else {
         ("all_gather_ms" if args.gather == "root" else "gather_to_rank0_ms"): timed(step_other, side_steps, 2)[0],
         "gemm_only_ms": timed(gemm_only, side_steps, 2)[0],
         "broadcast_only_ms": timed(broadcast_only, side_steps, 2)[0],
         "exchange_only_ms": timed(exchange_only, side_steps, 2)[0],
         "exchange_to_rank0_only_ms": timed(lambda: exchange_only(root=True), side_steps, 2)[0],
     }
+
+    # Timeline of one step (after two untimed ones): per event, ms from the
+    # step's start on each rank; rank 0's value and the largest over ranks.
+    trace = None
+    if use_ce:
+        plan_main, gather_main = (plan_root, gather_root) if args.gather == "root" else (plan, gather_all)
+        for _ in range(2):
+            step_main()
+        torch.cuda.synchronize()
+        dist.barrier()
+        marks = []
+        pipelined_step_ce(plan_main, a, pipe, gather_main, gemm, marks=marks)
+        torch.cuda.synchronize()
+        offsets = torch.tensor([marks[0][1].elapsed_time(event) for _, event in marks], device=device,
+                               dtype=torch.float64)
+        everyone = [torch.empty_like(offsets) for _ in range(world)]
+        dist.all_gather(everyone, offsets)
+        table = torch.stack(everyone).cpu()
+        trace = {"ms_from_step_start": {name: {"rank0": round(float(table[0, i]), 3),
+                                               "max": round(float(table[:, i].max()), 3)}
+                                        for i, (name, _) in enumerate(marks)},
+                 "marks": "gemm<i>: chunk i's GEMM done; exchange: this rank's pushes done; broadcast: the "
+                          "next step's B arrived; end: the step's last operation on the compute stream"}
 
     # FP64 check of rows received from a peer (its A shard is regenerated here
     # from the same seed): the GEMM and the exchange together.  All-gather: each
@@ -646,7 +669,7 @@ def multi_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
     del run_full, a_full
     native.set_sm_limit(gemm_sms if gemm_sms < sms else 0)
 
-    # End to end: pinned FP32 host A shard (every rank) and B (rank 0) -> device,
+    # End to end (skipped with --quick): pinned FP32 host A shard (every rank) and B (rank 0) -> device,
     # RNE conversion, the sharded step, the step's result back to pinned host
     # memory (gather to root: the whole C from rank 0; all-gather: each rank's rows).
     host_a = (torch.rand((stop - start, k), device=device) * 2 - 1).cpu().pin_memory()
@@ -666,7 +689,7 @@ def multi_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
         if host_c is not None:
             host_c.copy_(c_result, non_blocking=True)
 
-    e2e_ms, _ = timed(e2e_step, 3, 1)
+    e2e_ms = timed(e2e_step, 3, 1)[0] if not args.quick else float("nan")
     h2d = (stop - start) * k * 4 + (k * n * 4 if rank == 0 else 0)
     d2h = c_result.numel() * 4 if c_result is not None else 0
     del host_a, host_b, host_c, c_result, dev_a32, dev_b32
@@ -708,6 +731,7 @@ def multi_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
                "how": "the whole problem as one GEMM on each GPU at once, in the same run (max over GPUs)",
                "efficiency_vs_t1": t1_ms / (world * ms_per_step)},
         "breakdown_ms": breakdown,
+        "trace": trace,
         "bound": {"ingress_bytes_per_step_rank1": 2 * k * n + 4 * (m - (plan.rows[1][1] - plan.rows[1][0])) * n,
                   "ingress_bytes_per_step_rank0": 4 * (m - (stop - start)) * n,
                   "note": "every rank but 0 must receive one B (BF16) and the other ranks' C rows (FP32) per "

@@ -792,13 +792,16 @@ extern "C" int matmul_kernel_info(int implementation, int precision, char *json,
             "\"b_operand\":\"%s\",\"plan\":\"cost_model\",\"single_cta_kernel\":{\"tile_m\":%d,"
             "\"tile_n\":[256,128,64],\"buffering\":[%d,%d,%d],\"raster_group_m\":%d,"
             "\"split_k\":\"cluster_1x1xS_bulk_copy\",\"max_splits\":8},"
-            "\"pair_wide_kernel\":{\"tile_n\":%d,\"buffering\":%d,\"accumulator\":\"one, freed in column halves\"},\"skinny_kernel\":{\"when\":\"m<=64\",\"tile_n\":%d,\"max_splits\":8},"
+            "\"pair_wide_kernel\":{\"tile_n\":%d,\"buffering\":%d,\"accumulator\":\"one, freed in column halves\"},"
+            "\"pair_small_kernel\":{\"tile_n\":%d,\"buffering\":%d},"
+            "\"skinny_kernel\":{\"when\":\"m<=64\",\"tile_n\":%d,\"max_splits\":8},"
             "\"small_tf32\":\"ffma_tf32_rne when m*k*n<=2^25\"}",
             kPrecisionNames[precision], TC2_BM, TC2_BN, TC_ROW_BYTES / elem, TC_THREADS, TC2_HALF, TC2_BN, TC2_HALF,
             TC2_BN, TC2_STAGES, precision == kPrecTf32 ? "tf32" : "f16", TC2_BM, TC2_BN, 32 / elem,
-            TC_TMEM_COLUMNS, kRasterGroupMPair, precision == kPrecTf32 ? "rne by the TMA loads (TFLOAT32 tensor maps)" : "none",
+            TC_TMEM_COLUMNS, kRasterGroupMPair, precision == kPrecTf32 ? "rne_by_tma_tfloat32_loads" : "none",
             precision == kPrecTf32 ? "mn_major_tma_sw128_atom32B" : "mn_major_tma_sw128", TC_BM, TcTile<256>::kStages,
-            TcTile<128>::kStages, TcTile<64>::kStages, kRasterGroupM, TC2W_BN, Tc2Tile<TC2W_BN>::kStages, SK_BM);
+            TcTile<128>::kStages, TcTile<64>::kStages, kRasterGroupM, TC2W_BN, Tc2Tile<TC2W_BN>::kStages, TC2N_BN,
+            Tc2Tile<TC2N_BN>::kStages, SK_BM);
     } else {
         written = std::snprintf(
             json, json_size,

@@ -251,23 +251,51 @@ class CopyEngineGather:
         dist.all_reduce(self.token, group=self.group)
 
 
+def _timing_event(stream=None):
+    event = torch.cuda.Event(enable_timing=True)
+    event.record(stream)
+    return event
+
+
 def pipelined_step_ce(plan: ShardPlan, a_local: torch.Tensor, pipe: BroadcastPipeline, gather,
-                      gemm: Callable[[torch.Tensor, torch.Tensor, torch.Tensor], None]) -> None:
+                      gemm: Callable[[torch.Tensor, torch.Tensor, torch.Tensor], None],
+                      marks: list | None = None) -> None:
     """``pipelined_step`` with the C exchange of ``gather`` (``CopyEngineGather`` or
-    ``KernelPushGather``): each chunk is posted as soon as its GEMM is enqueued."""
+    ``KernelPushGather``): each chunk is posted as soon as its GEMM is enqueued.
+
+    With ``marks`` (a list), timing events are appended as (name, event) pairs:
+    "start", "gemm<i>" after chunk i's GEMM, "exchange" when this rank's pushes
+    are done, "broadcast" when the next B has arrived, "end" after the step.
+    """
+    if marks is not None:
+        marks.append(("start", _timing_event()))
     if plan.world > 1:
         pipe.start()
+        if marks is not None:
+            side = torch.cuda.Stream(device=a_local.device)
+            with torch.cuda.stream(side):
+                pipe.work.wait()
+                marks.append(("broadcast", _timing_event(side)))
     start, _ = plan.local_rows
     c_full = gather.c_full
     for index, (lo, hi) in enumerate(plan.chunk_ranges[plan.rank]):
         gemm(a_local[lo:hi], pipe.current, c_full[start + lo:start + hi])
         if plan.world > 1:
-            event = torch.cuda.Event()
+            event = torch.cuda.Event(enable_timing=marks is not None)
             event.record()
             gather.post(index, event)
+            if marks is not None:
+                marks.append((f"gemm{index}", event))
     if plan.world > 1:
+        if marks is not None:
+            side = torch.cuda.Stream(device=a_local.device)
+            for stream in getattr(gather, "streams", []) + ([gather.stream] if hasattr(gather, "stream") else []):
+                side.wait_stream(stream)
+            marks.append(("exchange", _timing_event(side)))
         gather.finish()
         pipe.finish()
+    if marks is not None:
+        marks.append(("end", _timing_event()))
 
 
 class KernelPushGather:
