@@ -218,21 +218,18 @@ cudaError_t pack_operands(const Context *ctx, const void *a, bool a_direct, void
                       stream, ja, jb, static_cast<int>(a_blocks));
 }
 
-// `pair` selects the CTA-pair kernel with a 256 x tile_n tile (tile_n = 64, 256
-// or 512), else the single-CTA kernel with a 128 x tile_n tile (256, 128 or 64).
+// tile_n selects the kernel: 0 = CTA pair with a 256 x 256 tile, 512 = CTA pair
+// with a 256 x 512 tile, else the single-CTA kernel with a 128 x tile_n tile.
 template <int FMT>
-cudaError_t launch_tc_kernel(bool pair, int tile_n, int splits, const CUtensorMap &ma, const CUtensorMap &mb,
+cudaError_t launch_tc_kernel(int tile_n, int splits, const CUtensorMap &ma, const CUtensorMap &mb,
                              const CUtensorMap &mc, const TcParams &params, int grid, cudaStream_t stream)
 {
     const dim3 block(TC_THREADS);
-    if (pair && tile_n == TC2_BN)
+    if (tile_n == 0)
         return launch_pdl(tc2_gemm_kernel<FMT, TC2_BN>, dim3(grid), block, Tc2Tile<TC2_BN>::kSmem, stream, ma, mb,
                           mc, params);
-    if (pair && tile_n == TC2W_BN)
+    if (tile_n == TC2W_BN)
         return launch_pdl(tc2_gemm_kernel<FMT, TC2W_BN>, dim3(grid), block, Tc2Tile<TC2W_BN>::kSmem, stream, ma,
-                          mb, mc, params);
-    if (pair)
-        return launch_pdl(tc2_gemm_kernel<FMT, TC2N_BN>, dim3(grid), block, Tc2Tile<TC2N_BN>::kSmem, stream, ma,
                           mb, mc, params);
     // Split K: one tile per cluster of `splits` CTAs along z.
     const dim3 g = splits > 1 ? dim3(static_cast<unsigned int>(params.num_tiles), 1, static_cast<unsigned int>(splits))
@@ -252,8 +249,7 @@ cudaError_t launch_tc_kernel(bool pair, int tile_n, int splits, const CUtensorMa
 }
 
 struct TcPlan {
-    bool pair;    // CTA pair (256 x tile_n: 64, 256 or 512) or single CTA (128 x tile_n: 256, 128 or 64)
-    int tile_n;
+    int tile_n;   // 0 = CTA pair (256 x 256), TC2W_BN = CTA pair (256 x 512), else the single-CTA tile width
     int splits;   // K splits (clusters of splits CTAs along z); single-CTA kernel only
 };
 
@@ -263,19 +259,18 @@ struct TcPlan {
 // most of its MMA time (2 x tile width cycles), its operand bytes at 55 B/cycle
 // into one SM, and all running CTAs' operand bytes at 8 KB/cycle out of L2; a
 // split adds 1000 cycles plus its shared-memory exchange at 8 B/cycle, and the
-// CTA pairs with 256- and 512-wide tiles 10000 cycles of start-up, the 64-wide
-// pair kPairSmallStart.  Fitted to measured B200 times of every option over
-// square, long-K, skinny and ragged shapes in BF16 and TF32 (the chosen plan is
-// within 3 % of the fastest on average).
-constexpr double kPairSmallStart = 2000.0;
-double tc_plan_cycles(const Context *ctx, int m, int k, int n, int prec, bool pair, int tile_n, int splits)
+// CTA pair 10000 cycles of start-up.  Fitted to measured B200 times of every
+// option over square, long-K, skinny and ragged shapes in BF16 and TF32 (the
+// chosen plan is within 3 % of the fastest on average).
+double tc_plan_cycles(const Context *ctx, int m, int k, int n, int prec, int tile_n, int splits)
 {
     constexpr double kStart = 2000.0, kEpilogue = 4000.0, kSmBytes = 55.0, kL2Bytes = 8000.0;
     const int64_t bk = prec == kPrecTf32 ? 32 : 64;
     const int64_t nkb = (static_cast<int64_t>(k) + bk - 1) / bk;
     int64_t tiles, rounds, active;
     double bytes_kb, mma;
-    const int pair_n = tile_n;
+    const bool pair = tile_n == 0 || tile_n == TC2W_BN;
+    const int pair_n = tile_n == TC2W_BN ? TC2W_BN : TC2_BN;
     if (pair) {
         tiles = ((static_cast<int64_t>(m) + TC2_BM - 1) / TC2_BM) * ((static_cast<int64_t>(n) + pair_n - 1) / pair_n);
         rounds = (tiles + ctx->max_pairs - 1) / ctx->max_pairs;
@@ -303,7 +298,7 @@ double tc_plan_cycles(const Context *ctx, int m, int k, int n, int prec, bool pa
     const double width = pair ? pair_n : tile_n;
     double cycles = kStart + static_cast<double>(rounds) * (static_cast<double>(kpb) * t_kb + kEpilogue * width / 256.0);
     if (pair)
-        cycles += pair_n == TC2N_BN ? kPairSmallStart : 10000.0;   // cluster launch, pair TMEM allocation, teardown
+        cycles += 10000.0;      // cluster launch, pair TMEM allocation and teardown
     if (splits > 1)
         cycles += 1000.0 + static_cast<double>(splits - 1) / splits * TC_BM * width * 4.0 / 8.0;
     return cycles;
@@ -313,20 +308,19 @@ TcPlan choose_tc_plan(const Context *ctx, int m, int k, int n, int prec)
 {
     const int elem = prec == kPrecTf32 ? 4 : 2;
     const int64_t nkb = (static_cast<int64_t>(k) + TC_ROW_BYTES / elem - 1) / (TC_ROW_BYTES / elem);
-    TcPlan best{false, 64, 1};
+    TcPlan best{64, 1};
     double best_cycles = 0.0;
-    auto consider = [&](bool pair, int tile_n, int splits) {
-        const double cycles = tc_plan_cycles(ctx, m, k, n, prec, pair, tile_n, splits);
+    auto consider = [&](int tile_n, int splits) {
+        const double cycles = tc_plan_cycles(ctx, m, k, n, prec, tile_n, splits);
         if (best_cycles == 0.0 || cycles < best_cycles) {
-            best = {pair, tile_n, splits};
+            best = {tile_n, splits};
             best_cycles = cycles;
         }
     };
     if (m > TC_BM && ctx->max_pairs > 0) {
-        consider(true, TC2_BN, 1);
+        consider(0, 1);
         if (n > TC2_BN)
-            consider(true, TC2W_BN, 1);
-        consider(true, TC2N_BN, 1);
+            consider(TC2W_BN, 1);
     }
     for (int tile_n : {256, 128, 64}) {
         const int64_t tiles =
@@ -341,7 +335,7 @@ TcPlan choose_tc_plan(const Context *ctx, int m, int k, int n, int prec)
                     (splits - 1) * kpb >= nkb)
                     continue;
             }
-            consider(false, tile_n, splits);
+            consider(tile_n, splits);
         }
     }
     return best;
@@ -501,12 +495,10 @@ int launch_tcgen05(Context *ctx, int prec, const void *a, const void *b, float *
     }
 
     const TcPlan plan = choose_tc_plan(ctx, m, k, n, prec);
-    const bool pair = plan.pair;
+    const int kernel_n = plan.tile_n;
+    const bool pair = kernel_n == 0 || kernel_n == TC2W_BN;
     const int tile_m = pair ? TC2_BM : TC_BM;
-    const int tile_n = plan.tile_n;
-    // The 64-wide pair tile stages 32-column B parts: 64-byte rows (64-byte
-    // swizzle) in FP16/BF16, one 128-byte TF32 box as in every other tile.
-    const bool b_sw64 = pair && tile_n == TC2N_BN && prec != kPrecTf32;
+    const int tile_n = kernel_n == 0 ? TC2_BN : kernel_n;
     const CUtensorMapDataType type = prec == kPrecTf32 ? CU_TENSOR_MAP_DATA_TYPE_TFLOAT32
                                      : prec == kPrecBf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                          : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -518,10 +510,8 @@ int launch_tcgen05(Context *ctx, int prec, const void *a, const void *b, float *
     bool ok = encode_2d(ctx, &map_a, type, a_op, static_cast<uint64_t>(k), static_cast<uint64_t>(m),
                         static_cast<uint64_t>(lda) * elem, bk, static_cast<uint32_t>(a_box_rows));
     ok = ok && encode_2d(ctx, &map_b, type, b_op, static_cast<uint64_t>(n), static_cast<uint64_t>(k),
-                         static_cast<uint64_t>(ldb) * elem, b_sw64 ? 32u : TC_ROW_BYTES / elem, bk,
-                         prec == kPrecTf32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
-                         : b_sw64          ? CU_TENSOR_MAP_SWIZZLE_64B
-                                           : CU_TENSOR_MAP_SWIZZLE_128B);
+                         static_cast<uint64_t>(ldb) * elem, TC_ROW_BYTES / elem, bk,
+                         prec == kPrecTf32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B);
     const bool c_direct = !(aligned16(c) && n % 4 == 0);
     if (ok && !c_direct)
         ok = encode_2d(ctx, &map_c, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, c, static_cast<uint64_t>(n),
@@ -559,11 +549,11 @@ int launch_tcgen05(Context *ctx, int prec, const void *a, const void *b, float *
 
     cudaError_t st;
     if (prec == kPrecTf32)
-        st = launch_tc_kernel<kFmtTF32>(pair, tile_n, plan.splits, map_a, map_b, map_c, params, grid, stream);
+        st = launch_tc_kernel<kFmtTF32>(kernel_n, plan.splits, map_a, map_b, map_c, params, grid, stream);
     else if (prec == kPrecBf16)
-        st = launch_tc_kernel<kFmtBF16>(pair, tile_n, plan.splits, map_a, map_b, map_c, params, grid, stream);
+        st = launch_tc_kernel<kFmtBF16>(kernel_n, plan.splits, map_a, map_b, map_c, params, grid, stream);
     else
-        st = launch_tc_kernel<kFmtF16>(pair, tile_n, plan.splits, map_a, map_b, map_c, params, grid, stream);
+        st = launch_tc_kernel<kFmtF16>(kernel_n, plan.splits, map_a, map_b, map_c, params, grid, stream);
     if (pooled)
         cudaFreeAsync(pooled, stream);
     if (st != cudaSuccess)
@@ -792,16 +782,13 @@ extern "C" int matmul_kernel_info(int implementation, int precision, char *json,
             "\"b_operand\":\"%s\",\"plan\":\"cost_model\",\"single_cta_kernel\":{\"tile_m\":%d,"
             "\"tile_n\":[256,128,64],\"buffering\":[%d,%d,%d],\"raster_group_m\":%d,"
             "\"split_k\":\"cluster_1x1xS_bulk_copy\",\"max_splits\":8},"
-            "\"pair_wide_kernel\":{\"tile_n\":%d,\"buffering\":%d,\"accumulator\":\"one, freed in column halves\"},"
-            "\"pair_small_kernel\":{\"tile_n\":%d,\"buffering\":%d},"
-            "\"skinny_kernel\":{\"when\":\"m<=64\",\"tile_n\":%d,\"max_splits\":8},"
+            "\"pair_wide_kernel\":{\"tile_n\":%d,\"buffering\":%d,\"accumulator\":\"one, freed in column halves\"},\"skinny_kernel\":{\"when\":\"m<=64\",\"tile_n\":%d,\"max_splits\":8},"
             "\"small_tf32\":\"ffma_tf32_rne when m*k*n<=2^25\"}",
             kPrecisionNames[precision], TC2_BM, TC2_BN, TC_ROW_BYTES / elem, TC_THREADS, TC2_HALF, TC2_BN, TC2_HALF,
             TC2_BN, TC2_STAGES, precision == kPrecTf32 ? "tf32" : "f16", TC2_BM, TC2_BN, 32 / elem,
             TC_TMEM_COLUMNS, kRasterGroupMPair, precision == kPrecTf32 ? "rne_by_tma_tfloat32_loads" : "none",
             precision == kPrecTf32 ? "mn_major_tma_sw128_atom32B" : "mn_major_tma_sw128", TC_BM, TcTile<256>::kStages,
-            TcTile<128>::kStages, TcTile<64>::kStages, kRasterGroupM, TC2W_BN, Tc2Tile<TC2W_BN>::kStages, TC2N_BN,
-            Tc2Tile<TC2N_BN>::kStages, SK_BM);
+            TcTile<128>::kStages, TcTile<64>::kStages, kRasterGroupM, TC2W_BN, Tc2Tile<TC2W_BN>::kStages, SK_BM);
     } else {
         written = std::snprintf(
             json, json_size,
@@ -973,10 +960,7 @@ extern "C" void *matmul_create(int device, char *error, size_t error_size)
         {reinterpret_cast<const void *>(&tc2_gemm_kernel<kFmtTF32, TC2_BN>), Tc2Tile<TC2_BN>::kSmem},
         {reinterpret_cast<const void *>(&tc2_gemm_kernel<kFmtF16, TC2W_BN>), Tc2Tile<TC2W_BN>::kSmem},
         {reinterpret_cast<const void *>(&tc2_gemm_kernel<kFmtBF16, TC2W_BN>), Tc2Tile<TC2W_BN>::kSmem},
-        {reinterpret_cast<const void *>(&tc2_gemm_kernel<kFmtTF32, TC2W_BN>), Tc2Tile<TC2W_BN>::kSmem},
-        {reinterpret_cast<const void *>(&tc2_gemm_kernel<kFmtF16, TC2N_BN>), Tc2Tile<TC2N_BN>::kSmem},
-        {reinterpret_cast<const void *>(&tc2_gemm_kernel<kFmtBF16, TC2N_BN>), Tc2Tile<TC2N_BN>::kSmem},
-        {reinterpret_cast<const void *>(&tc2_gemm_kernel<kFmtTF32, TC2N_BN>), Tc2Tile<TC2N_BN>::kSmem}};
+        {reinterpret_cast<const void *>(&tc2_gemm_kernel<kFmtTF32, TC2W_BN>), Tc2Tile<TC2W_BN>::kSmem}};
     for (const auto &kernel : tc2_kernels) {
         st = cudaFuncSetAttribute(kernel.first, cudaFuncAttributeMaxDynamicSharedMemorySize, kernel.second);
         if (st != cudaSuccess) {
@@ -985,9 +969,9 @@ extern "C" void *matmul_create(int device, char *error, size_t error_size)
             return nullptr;
         }
     }
-    // How many 2-CTA clusters of the pair kernels (every width) fit on the device at once.
+    // How many 2-CTA clusters of the pair kernels (both widths) fit on the device at once.
     ctx->max_pairs = -1;
-    for (int i : {1, 4, 7}) {
+    for (int i : {1, 4}) {
         cudaLaunchConfig_t config{};
         config.gridDim = dim3(2 * (sms / 2), 1, 1);
         config.blockDim = dim3(TC_THREADS, 1, 1);
@@ -1142,9 +1126,9 @@ extern "C" int matmul_plan(void *opaque, int implementation, int precision, int 
                                 m <= 16 ? 16 : m <= 32 ? 32 : 64, SK_BM, skinny_splits(ctx, n, total_k_blocks));
     } else {
         const TcPlan plan = choose_tc_plan(ctx, m, k, n, precision);
-        const bool pair = plan.pair;
+        const bool pair = plan.tile_n == 0 || plan.tile_n == TC2W_BN;
         const int tile_m = pair ? TC2_BM : TC_BM;
-        const int tile_n = plan.tile_n;
+        const int tile_n = plan.tile_n == 0 ? TC2_BN : plan.tile_n;
         const int64_t tiles = ((static_cast<int64_t>(m) + tile_m - 1) / tile_m) *
                               ((static_cast<int64_t>(n) + tile_n - 1) / tile_n);
         const int64_t ctas = pair ? 2 * (tiles < ctx->max_pairs ? tiles : ctx->max_pairs)

@@ -1,19 +1,13 @@
 // CTA-pair (cta_group::2) variant of the tcgen05 GEMM: one 2-CTA cluster computes
-// a 256 x BN output tile (BN = 64, 256 or 512) with tcgen05.mma.cta_group::2
-// instructions of M = 256, N = min(BN, 256) (BN / N of them per K step).
+// a 256 x BN output tile (BN = 256 or 512) with tcgen05.mma.cta_group::2
+// instructions of M = 256, N = 256 (BN / 256 of them per K step).
 //
 // Split of the tile across the pair (rank r = %cluster_ctarank, 0 = leader):
 //   * A: CTA r stages rows [m0 + 128 r, m0 + 128 r + 128) of the K slice;
-//   * B: for each N-column part h of the tile, CTA r stages columns
-//     [n0 + N h + (N / 2) r, + N / 2);
+//   * B: for each 256-column half h of the tile, CTA r stages columns
+//     [n0 + 256 h + 128 r, +128);
 //   * D: CTA r's TMEM holds output rows m0 + 128 r .. +127, all BN columns
 //     (TMEM column c = output column n0 + c).
-// BN = 64 is the small-problem tile: it halves the B bytes each SM stages per K
-// block against a 128 x 64 single-CTA tile (20 KB instead of 24 KB), the rate
-// that bounds GEMMs of a few thousand tiles or fewer.  Each CTA's 32-column B
-// half is 64 bytes wide in FP16/BF16, so it is staged with the 64-byte swizzle
-// (TMA box 32 columns x 64 k-rows; 8-row atoms of 512 bytes); TF32's 32 columns
-// are one 128-byte box as in the wider tiles.
 // Both CTAs keep their operands at the same shared-memory offsets; the leader's
 // descriptors name its own copy and the tensor cores of the pair read both.
 //
@@ -56,28 +50,23 @@
 namespace b200 {
 
 constexpr int TC2_BM = 256;                 // rows per pair tile
-constexpr int TC2_BN = 256;                 // columns per pair tile (square kernel)
+constexpr int TC2_BN = 256;                 // columns per pair tile (narrow kernel)
 constexpr int TC2W_BN = 512;                // columns per pair tile (wide kernel)
-constexpr int TC2N_BN = 64;                 // columns per pair tile (small-problem kernel)
-constexpr int TC2_HALF = 128;               // rows of A staged per CTA
+constexpr int TC2_HALF = 128;               // rows (A) / columns of a B half staged per CTA
 constexpr int TC2_A_STAGE = TC2_HALF * TC_ROW_BYTES;   // 16 KB
 
 template <int BN>
 struct Tc2Tile {
-    static_assert(BN == 64 || BN == 256 || BN == 512, "pair tile width");
-    static constexpr int kMmaN = BN < 256 ? BN : 256;               // N of one MMA
-    static constexpr int kHalves = BN / kMmaN;                      // MMAs per K step
-    static constexpr int kCols = kMmaN / 2;                         // B columns per CTA and MMA
-    static constexpr int kBStage = kHalves * kCols * TC_ROW_BYTES;  // 4, 16 or 32 KB
-    static constexpr int kStages = BN == 64 ? 8 : BN == 256 ? 6 : 4;
-    static constexpr int kAccs = BN == 512 ? 1 : 2;                 // TMEM accumulators of BN columns
-    static constexpr uint32_t kTmemColumns = BN == 64 ? 128 : 512;
+    static_assert(BN == 256 || BN == 512, "pair tile width");
+    static constexpr int kHalves = BN / 256;                        // N = 256 MMAs per K step
+    static constexpr int kBStage = kHalves * TC2_HALF * TC_ROW_BYTES;   // 16 or 32 KB
+    static constexpr int kStages = BN == 256 ? 6 : 4;
+    static constexpr int kAccs = BN == 256 ? 2 : 1;                 // TMEM accumulators of BN columns
     static constexpr int kSmem = 1024 + kStages * (TC2_A_STAGE + kBStage) + TC_EPI_BYTES + TC_BAR_BYTES;
 };
 constexpr int TC2_STAGES = Tc2Tile<TC2_BN>::kStages;
 constexpr int TC2_SMEM_BYTES = Tc2Tile<TC2_BN>::kSmem;
 static_assert(Tc2Tile<TC2W_BN>::kSmem <= 227 * 1024, "wide pair tile exceeds shared memory");
-static_assert(Tc2Tile<TC2N_BN>::kSmem <= 227 * 1024, "small pair tile exceeds shared memory");
 
 template <int FMT, int BN = TC2_BN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
@@ -86,9 +75,7 @@ tc2_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
 {
     using Tile = Tc2Tile<BN>;
     constexpr int kStages = Tile::kStages;
-    constexpr int kMmaN = Tile::kMmaN;
     constexpr int kHalves = Tile::kHalves;
-    constexpr int kCols = Tile::kCols;
     constexpr int kBStage = Tile::kBStage;
     constexpr int kAccs = Tile::kAccs;
     constexpr int kDefer = 2;     // BN = 512: K blocks at each end of a tile run on one column half first
@@ -98,15 +85,11 @@ tc2_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
     constexpr int kBK = TC_ROW_BYTES / kElem;          // K elements per stage (64 or 32)
     constexpr int kMmaK = 32 / kElem;                  // K per instruction (16 or 8)
     constexpr int kMmasPerStage = kBK / kMmaK;         // 4
-    // MN-major B boxes: 128-byte rows (64 FP16/BF16 or 32 TF32 columns), or for
-    // the 64-wide tile in FP16/BF16 64-byte rows of 32 columns (64-byte swizzle).
-    constexpr bool kSw64 = kCols * kElem < TC_ROW_BYTES;
-    constexpr int kNB = kSw64 ? kCols : TC_ROW_BYTES / kElem;   // B box width in elements
-    constexpr int kBBoxes = kCols / kNB;               // boxes per CTA part (MN-major B)
-    constexpr uint32_t kBRowBytes = kNB * kElem;       // bytes per k-row of a box
-    constexpr uint32_t kBBoxBytes = kBK * kBRowBytes;
-    constexpr uint32_t kIdesc = tc_instr_desc(FMT, false, TC2_BM, kMmaN);   // B MN-major in every format
-    constexpr uint32_t kBHalfBytes = kCols * TC_ROW_BYTES;            // one CTA's B part of one MMA
+    constexpr int kNB = TC_ROW_BYTES / kElem;          // MN-major B box width (64)
+    constexpr int kBBoxes = TC2_HALF / kNB;            // 2 boxes per CTA half (MN-major B)
+    constexpr uint32_t kBBoxBytes = kBK * TC_ROW_BYTES;
+    constexpr uint32_t kIdesc = tc_instr_desc(FMT, false, TC2_BM, 256);   // B MN-major in every format
+    constexpr uint32_t kBHalfBytes = TC2_HALF * TC_ROW_BYTES;         // one 128-column B half of a CTA
     constexpr uint32_t kStageTx = 2u * (TC2_A_STAGE + kBStage);       // both CTAs
 
     extern __shared__ uint8_t smem_raw[];
@@ -150,7 +133,7 @@ tc2_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
             tma_prefetch_map(&map_c);
     }
     if (warp == 1) {
-        tmem_alloc_pair(tmem_slot, Tile::kTmemColumns);
+        tmem_alloc_pair(tmem_slot, TC_TMEM_COLUMNS);
         tmem_relinquish_pair();
     }
     tc_fence_before();
@@ -173,7 +156,7 @@ tc2_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
                 int mb, nb;
                 tc_tile_coords(tile, p, mb, nb);
                 const int a_row = mb * TC2_BM + static_cast<int>(rank) * TC2_HALF;
-                const int b_col = nb * BN + static_cast<int>(rank) * kCols;
+                const int b_col = nb * BN + static_cast<int>(rank) * TC2_HALF;
                 for (int kb = 0; kb < p.num_k_blocks; ++kb) {
                     if (!mbar_wait(empty_bar(stage), phase ^ 1u)) {
                         report_status(kStatusLoadTimeout);
@@ -189,7 +172,7 @@ tc2_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
                         const uint32_t s_bh = s_b + stage * kBStage + h * kBHalfBytes;
 #pragma unroll
                         for (int j = 0; j < kBBoxes; ++j)
-                            tma_load_2d_pair(s_bh + j * kBBoxBytes, &map_b, fb, b_col + h * kMmaN + j * kNB, kb * kBK);
+                            tma_load_2d_pair(s_bh + j * kBBoxBytes, &map_b, fb, b_col + h * 256 + j * kNB, kb * kBK);
                     }
                     filled |= 1u << stage;
                     fill_parity = (fill_parity & ~(1u << stage)) | (phase << stage);
@@ -215,21 +198,19 @@ tc2_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
             // Loop-invariant descriptor halves: only the start-address field (bits 0-13,
             // address >> 4) moves between stages and K slices, so the issue loop adds.
             const uint64_t a_desc0 = smem_desc_sw128(s_a, 16, 1024);
-            // 64-byte swizzle (layout type 4): 8 k-rows of 64 bytes per atom, atoms
-            // 512 bytes apart along K; one atom across the 32 columns.
-            const uint64_t b_desc0 = kSw64 ? smem_desc(s_b, kBBoxBytes, 512u, 4u) : smem_desc_mn<kTF32>(s_b, kBBoxBytes);
+            const uint64_t b_desc0 = smem_desc_mn<kTF32>(s_b, kBBoxBytes);
             constexpr uint64_t kADescStage = TC2_A_STAGE >> 4;
             constexpr uint64_t kBDescStage = kBStage >> 4;
             constexpr uint64_t kBDescHalf = kBHalfBytes >> 4;
             constexpr uint64_t kADescK = 32 >> 4;
-            constexpr uint64_t kBDescK = (kMmaK * kBRowBytes) >> 4;
-            // The MMAs of one K block for one N-column part h of the accumulator.
+            constexpr uint64_t kBDescK = (kMmaK * TC_ROW_BYTES) >> 4;
+            // The MMAs of one K block for one 256-column half of the accumulator.
             auto issue_half = [&](uint32_t d_tmem, int s, int h, int kb) {
                 const uint64_t a_desc = a_desc0 + static_cast<uint64_t>(s) * kADescStage;
                 const uint64_t b_desc = b_desc0 + static_cast<uint64_t>(s) * kBDescStage + h * kBDescHalf;
 #pragma unroll
                 for (int kk = 0; kk < kMmasPerStage; ++kk)
-                    tc_mma_pair<kTF32>(d_tmem + static_cast<uint32_t>(h * kMmaN), a_desc + kk * kADescK,
+                    tc_mma_pair<kTF32>(d_tmem + static_cast<uint32_t>(h * 256), a_desc + kk * kADescK,
                                        b_desc + kk * kBDescK, kIdesc, (kb | kk) != 0 ? 1u : 0u);
             };
             int acc = 0;
@@ -345,8 +326,8 @@ tc2_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
                 }
                 uint32_t v[32];
                 tmem_load_32cols(t_row + chunk * 32, v);
-                if (chunk % (kMmaN / 32) == kMmaN / 32 - 1) {
-                    // Accumulator `acc` (BN = 64, 256) or column half chunk / 8 (BN = 512) read.
+                if (chunk % 8 == 7) {
+                    // Accumulator `acc` (BN = 256) or column half chunk / 8 (BN = 512) read.
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0)
@@ -428,7 +409,7 @@ tc2_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
     cluster_sync_all();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc_pair(tmem_base, Tile::kTmemColumns);
+        tmem_dealloc_pair(tmem_base, TC_TMEM_COLUMNS);
     }
 }
 
