@@ -772,7 +772,9 @@ def main() -> int:
                              "in the same run")
     parser.add_argument("--ce-streams", type=int, default=1,
                         help="copy streams of the copy-engine exchange (peers visited rank+1, rank+2, ...)")
-    parser.add_argument("--quick", action="store_true", help="skip the per-precision and cuBLAS tables")
+    parser.add_argument("--quick", action="store_true",
+                        help="skip the per-precision and cuBLAS tables (one GPU) or the per-part breakdown and the "
+                             "end-to-end step (several GPUs)")
     parser.add_argument("--sweep", choices=("square", "llm", "ragged", "all", "legacy"), default=None,
                         help="instead of the contract line, time every shape of a configuration "
                              "(reference graph method, one JSON line per case, torch/cuBLAS beside it); "
