@@ -672,27 +672,30 @@ def multi_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
     # End to end (skipped with --quick): pinned FP32 host A shard (every rank) and B (rank 0) -> device,
     # RNE conversion, the sharded step, the step's result back to pinned host
     # memory (gather to root: the whole C from rank 0; all-gather: each rank's rows).
-    host_a = (torch.rand((stop - start, k), device=device) * 2 - 1).cpu().pin_memory()
-    host_b = (torch.rand((k, n), device=device) * 2 - 1).cpu().pin_memory() if rank == 0 else None
     c_result = (c if rank == 0 else None) if args.gather == "root" else c[start:stop]
-    host_c = torch.empty(c_result.shape, dtype=torch.float32).pin_memory() if c_result is not None else None
-    dev_a32 = torch.empty((stop - start, k), dtype=torch.float32, device=device)
-    dev_b32 = torch.empty((k, n), dtype=torch.float32, device=device) if rank == 0 else None
-
-    def e2e_step():
-        dev_a32.copy_(host_a, non_blocking=True)
-        native.convert(dev_a32, a, "bf16")
-        if rank == 0:
-            dev_b32.copy_(host_b, non_blocking=True)
-            native.convert(dev_b32, pipe.pending, "bf16")
-        step_main()
-        if host_c is not None:
-            host_c.copy_(c_result, non_blocking=True)
-
-    e2e_ms = timed(e2e_step, 3, 1)[0] if not args.quick else float("nan")
     h2d = (stop - start) * k * 4 + (k * n * 4 if rank == 0 else 0)
     d2h = c_result.numel() * 4 if c_result is not None else 0
-    del host_a, host_b, host_c, c_result, dev_a32, dev_b32
+    e2e_ms = float("nan")
+    if not args.quick:
+        host_a = (torch.rand((stop - start, k), device=device) * 2 - 1).cpu().pin_memory()
+        host_b = (torch.rand((k, n), device=device) * 2 - 1).cpu().pin_memory() if rank == 0 else None
+        host_c = torch.empty(c_result.shape, dtype=torch.float32).pin_memory() if c_result is not None else None
+        dev_a32 = torch.empty((stop - start, k), dtype=torch.float32, device=device)
+        dev_b32 = torch.empty((k, n), dtype=torch.float32, device=device) if rank == 0 else None
+
+        def e2e_step():
+            dev_a32.copy_(host_a, non_blocking=True)
+            native.convert(dev_a32, a, "bf16")
+            if rank == 0:
+                dev_b32.copy_(host_b, non_blocking=True)
+                native.convert(dev_b32, pipe.pending, "bf16")
+            step_main()
+            if host_c is not None:
+                host_c.copy_(c_result, non_blocking=True)
+
+        e2e_ms = timed(e2e_step, 3, 1)[0]
+        del host_a, host_b, host_c, dev_a32, dev_b32
+    del c_result
 
     status = native.device_status()
     status_t = torch.tensor([status], device=device, dtype=torch.int64)
