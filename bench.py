@@ -367,9 +367,24 @@ def single_gpu(args) -> dict:
         host_gemm(host_a, host_b, host_c)
     e2e_ms = (time.perf_counter() - wall_e0) * 1e3 / e2e_steps
     check["e2e_max_abs_diff_vs_device_path"] = float((host_c - c.cpu()).abs().max().item())
+    # The link's own floor for this call: the same host-to-device bytes alone, and
+    # the C copy back alone (pinned buffers, one copy stream, wall clock).
+    link = {}
+    for label, copies in (("h2d_only_ms", ((host_gemm.b32, host_b), (host_gemm.a32, host_a))),
+                          ("d2h_only_ms", ((host_c, host_gemm.c),))):
+        times = []
+        for _ in range(3):
+            t0 = time.perf_counter()
+            with torch.cuda.stream(host_gemm.copy_in):
+                for dst, src in copies:
+                    dst.copy_(src, non_blocking=True)
+            host_gemm.copy_in.synchronize()
+            times.append((time.perf_counter() - t0) * 1e3)
+        link[label] = min(times)
     e2e = {"value": tflops(m, k, n, e2e_ms), "unit": "TFLOP/s",
            "h2d_bytes_per_step": host_gemm.bytes_in, "d2h_bytes_per_step": host_gemm.bytes_out,
            "ms_per_step": e2e_ms, "steps": e2e_steps, "timing": "host wall clock per call (the call synchronizes)",
+           "link_ms": link,
            "path": "HostMatmul: pinned FP32 host A,B -> H2D (B, then A in 8 row blocks, the last split in 2) -> matmul_convert "
                    "(RNE to BF16) -> matmul_launch per block -> D2H of each C block overlapping later H2D"}
     del host_a, host_b, host_c, host_gemm
