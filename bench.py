@@ -778,7 +778,7 @@ def main() -> int:
     parser.add_argument("--workload", choices=("square8192", "rowshard32768"), default=None)
     parser.add_argument("--size", type=int, default=None, help="override the sharded problem size")
     parser.add_argument("--chunks", type=int, default=8)
-    parser.add_argument("--reserve-sms", type=int, default=16,
+    parser.add_argument("--reserve-sms", type=int, default=8,
                         help="multi-GPU: SMs left free of GEMM CTAs for the NCCL kernels that overlap them")
     parser.add_argument("--exchange", choices=("ce", "push", "nccl"), default="ce",
                         help="multi-GPU C exchange: copy-engine pushes over symmetric memory, this library's "
