@@ -491,8 +491,8 @@ def multi_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
     import torch.distributed as dist
 
     from gpumat import NativeMatmul
-    from sharded import (BroadcastPipeline, CopyEngineGather, KernelPushGather, ShardPlan, pipelined_step,
-                         pipelined_step_ce)
+    from sharded import (BroadcastPipeline, CopyEngineBroadcast, CopyEngineGather, KernelPushGather, ShardPlan,
+                         pipelined_step, pipelined_step_ce)
 
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
@@ -516,7 +516,15 @@ def multi_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
         return out
 
     a = shard_a(rank)
-    b = torch.empty((k, n), dtype=torch.bfloat16, device=device)
+    if args.broadcast == "ce":
+        import torch.distributed._symmetric_memory as symm_mem
+
+        # Both B buffers in symmetric memory: every rank maps every peer's copies.
+        b = symm_mem.empty((k, n), dtype=torch.bfloat16, device=device)
+        b_next = symm_mem.empty((k, n), dtype=torch.bfloat16, device=device)
+        b_handles = [symm_mem.rendezvous(b, dist.group.WORLD), symm_mem.rendezvous(b_next, dist.group.WORLD)]
+    else:
+        b = torch.empty((k, n), dtype=torch.bfloat16, device=device)
     if rank == 0:
         gen = torch.Generator(device=device)
         gen.manual_seed(7)
@@ -541,7 +549,12 @@ def multi_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
     else:
         c = torch.empty((m, n), dtype=torch.float32, device=device)
     dist.broadcast(b, src=0)                            # the first step's B, before the loop
-    pipe = BroadcastPipeline(b, b_group)
+    if args.broadcast == "ce":
+        b_next.copy_(b)                                 # rank 0: the next step's B (the same matrix here)
+        pipe = CopyEngineBroadcast(b, b_next, b_group, b_handles)
+        del b_next
+    else:
+        pipe = BroadcastPipeline(b, b_group)
     del b
     sms = torch.cuda.get_device_properties(device).multi_processor_count
     gemm_sms = max(2, sms - args.reserve_sms) if args.reserve_sms else sms
@@ -719,6 +732,9 @@ def multi_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
     native.close()
     if use_ce:
         del gather_all, gather_root, handle
+    del pipe
+    if args.broadcast == "ce":
+        del b_handles
     dist.barrier()
     dist.destroy_process_group()
     if rank != 0:
@@ -736,6 +752,10 @@ def multi_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
                                   + f" in {plan.chunk_count} row chunks, each chunk's exchange overlapping the "
                                   f"next chunk's GEMM",
                    "gather": args.gather,
+                   "broadcast": ("copy-engine pushes over symmetric memory: rank 0 sends part j of B to rank j+1, "
+                                 "a one-element all-reduce, each owner forwards its part to the other ranks, a "
+                                 "second all-reduce at the end of the step") if args.broadcast == "ce"
+                                else "NCCL broadcast on its own communicator",
                    "exchange": ("copy-engine pushes into the peers' C (symmetric memory, one cudaMemcpyAsync "
                                 f"per peer and chunk, peers rank+1, rank+2, ... on {args.ce_streams} copy "
                                 "stream(s)), completed by a one-element NCCL all-reduce")
@@ -784,6 +804,9 @@ def main() -> int:
                         help="multi-GPU C exchange: copy-engine pushes over symmetric memory, this library's "
                              "push kernel over symmetric memory, or NCCL send/recv")
     parser.add_argument("--push-ctas", type=int, default=16, help="CTAs of the push kernel (--exchange push)")
+    parser.add_argument("--broadcast", choices=("nccl", "ce"), default="nccl",
+                        help="multi-GPU B broadcast: NCCL on its own communicator, or copy-engine pushes over "
+                             "symmetric memory (rank 0 scatters B's parts, their owners forward them)")
     parser.add_argument("--gather", choices=("root", "all"), default="root",
                         help="multi-GPU: where C is assembled in the timed step -- on rank 0 (the single-GPU "
                              "call's result, on one device) or on every rank; the other variant is timed "

@@ -14,6 +14,9 @@ The reference is single-device (src/benchmark_backends.py selects one
   step ahead (double-buffered B), so it too overlaps the GEMMs; the GEMMs are
   then launched on fewer SMs than the device has (``matmul_set_sm_limit``) so
   that the communication kernels find free SMs while they run;
+  ``CopyEngineBroadcast`` does the same broadcast with copy-engine pushes over
+  symmetric memory (rank 0 scatters B's parts, their owners forward them), so
+  only two one-element all-reduces per step need an SM;
 * with ``CopyEngineGather`` the C exchange takes no SM at all: C lives in
   symmetric memory (every rank maps every peer's C), and each finished chunk
   is pushed into the peers' C by copy-engine transfers (one cudaMemcpyAsync per
@@ -151,12 +154,115 @@ class BroadcastPipeline:
             raise RuntimeError("broadcast already in flight")
         self.work = dist.broadcast(self.pending, src=0, group=self.group, async_op=True)
 
+    def join(self, stream=None) -> None:
+        """Make ``stream`` (default: the current one) wait for the broadcast in flight."""
+        if self.work is None:
+            raise RuntimeError("no broadcast in flight")
+        with torch.cuda.stream(stream or torch.cuda.current_stream(self.current.device)):
+            self.work.wait()
+
     def finish(self) -> None:
         if self.work is None:
             raise RuntimeError("no broadcast in flight")
         self.work.wait()
         self.work = None
         self.current, self.pending = self.pending, self.current
+
+
+def broadcast_parts(k: int, world: int) -> list[tuple[int, int]]:
+    """Row ranges of B's parts for ``CopyEngineBroadcast``: part j (rows of B, in
+    order) belongs to rank j + 1; rank 0 holds B and owns none."""
+    return chunk_rows(k, world - 1) if world > 1 else []
+
+
+class CopyEngineBroadcast:
+    """``BroadcastPipeline`` with the transfers done by copy engines instead of NCCL kernels.
+
+    ``current`` and ``pending`` must come from
+    ``torch.distributed._symmetric_memory.empty`` on every rank (same shape), with
+    their rendezvous handles.  ``start()`` sends rank 0's ``pending`` (the next
+    step's B) to every rank in two phases on a side stream, taking no SM:
+
+    1. rank 0 pushes part j of B (``broadcast_parts``) into rank j + 1's
+       ``pending`` only, so each row of B leaves rank 0 once;
+    2. after a one-element all-reduce on ``group`` (every part has landed), each
+       rank j + 1 pushes its part into every other rank's ``pending``.
+
+    ``finish()`` makes the current stream wait for this rank's pushes, runs a
+    second one-element all-reduce (every rank's pushes are done, so every
+    ``pending`` is whole) and swaps the buffers.  Rank 0 egresses one B, every
+    other rank receives one B, and no kernel runs on the SMs the GEMM uses apart
+    from the two small all-reduces.
+    """
+
+    def __init__(self, current: torch.Tensor, pending: torch.Tensor, group, handles, *, copy=None,
+                 new_stream=None, world: int | None = None, rank: int | None = None):
+        self.current, self.pending = current, pending
+        self.group = group
+        self.world = dist.get_world_size(group) if world is None else world
+        self.rank = dist.get_rank(group) if rank is None else rank
+        self.copy = copy if copy is not None else _memcpy_d2d
+        shape, dtype = tuple(current.shape), current.dtype
+        # handles[i] is the rendezvous handle of buffer i (0: the initial current, 1: the initial pending).
+        self.peer_views = [{peer: handle.get_buffer(peer, shape, dtype) for peer in range(self.world)
+                            if peer != self.rank} for handle in handles]
+        self.local = [current, pending]
+        self.which = 1                    # index of the buffer that is pending now
+        self.row_bytes = current.shape[1] * current.element_size()
+        self.parts = broadcast_parts(current.shape[0], self.world)
+        self.stream = (new_stream or (lambda: torch.cuda.Stream(device=current.device)))()
+        self.token = torch.zeros(1, dtype=torch.float32, device=current.device)
+        self.in_flight = False
+
+    def _push(self, part: int, peers) -> None:
+        lo, hi = self.parts[part]
+        if hi <= lo:
+            return
+        src = self.local[self.which].data_ptr() + lo * self.row_bytes
+        for peer in peers:
+            dst = self.peer_views[self.which][peer].data_ptr() + lo * self.row_bytes
+            self.copy(dst, src, (hi - lo) * self.row_bytes, self.stream)
+
+    def scatter(self) -> None:
+        """Phase 1 (rank 0): part j of the pending B into rank j + 1's pending buffer."""
+        if self.rank == 0:
+            for part in range(len(self.parts)):
+                self._push(part, [part + 1])
+
+    def forward(self) -> None:
+        """Phase 2 (rank j + 1): part j into every other rank's pending buffer but rank 0's,
+        peers in the order rank + 1, rank + 2, ..."""
+        if 0 < self.rank <= len(self.parts):       # B with fewer rows than ranks leaves some without a part
+            order = [(self.rank + d) % self.world for d in range(1, self.world)]
+            self._push(self.rank - 1, [peer for peer in order if peer != 0])
+
+    def start(self) -> None:
+        if self.in_flight:
+            raise RuntimeError("broadcast already in flight")
+        self.in_flight = True
+        if self.world < 2:
+            return
+        # The pending buffer is free on every rank: the previous step ended with an
+        # all-reduce that followed every rank's GEMMs.
+        self.stream.wait_stream(torch.cuda.current_stream(self.current.device))
+        with torch.cuda.stream(self.stream):
+            self.scatter()
+            dist.all_reduce(self.token, group=self.group)
+            self.forward()
+
+    def join(self, stream=None) -> None:
+        """Make ``stream`` (default: the current one) wait for this rank's pushes."""
+        (stream or torch.cuda.current_stream(self.current.device)).wait_stream(self.stream)
+
+    def finish(self) -> None:
+        if not self.in_flight:
+            raise RuntimeError("no broadcast in flight")
+        self.in_flight = False
+        if self.world > 1:
+            self.join()
+            dist.all_reduce(self.token, group=self.group)
+        self.which ^= 1
+        self.current, self.pending = self.local[self.which ^ 1], self.local[self.which]
 
 
 def pipelined_step(plan: ShardPlan, a_local: torch.Tensor, pipe: BroadcastPipeline, c_full: torch.Tensor,
@@ -273,9 +379,8 @@ def pipelined_step_ce(plan: ShardPlan, a_local: torch.Tensor, pipe: BroadcastPip
         pipe.start()
         if marks is not None:
             side = torch.cuda.Stream(device=a_local.device)
-            with torch.cuda.stream(side):
-                pipe.work.wait()
-                marks.append(("broadcast", _timing_event(side)))
+            pipe.join(side)
+            marks.append(("broadcast", _timing_event(side)))
     start, _ = plan.local_rows
     c_full = gather.c_full
     for index, (lo, hi) in enumerate(plan.chunk_ranges[plan.rank]):

@@ -247,3 +247,40 @@ def test_kernel_push_gather_places_every_chunk(world, m, chunks, gather):
         if gather == "all" or r == 0:
             assert torch.equal(buffers[r], expected), r
     assert max(calls) == (world - 1 if gather == "all" else 1)
+
+
+@pytest.mark.parametrize("world,k", [(2, 7), (3, 10), (4, 9), (8, 100), (8, 5)])
+def test_copy_engine_broadcast_delivers_b_to_every_rank(world, k):
+    """CopyEngineBroadcast's two phases: after rank 0's scatter and every owner's
+    forward, each rank's pending buffer holds rank 0's B, rank 0 sent each row of B
+    exactly once, and the current buffers are untouched (all ranks in one process,
+    host buffers standing in for the peers' mapped buffers, memmove for the copy)."""
+    import ctypes
+
+    from sharded import CopyEngineBroadcast, broadcast_parts
+
+    n = 3
+    b_next = torch.arange(k * n, dtype=torch.float32).reshape(k, n)
+    currents = [torch.full((k, n), 7.0) for _ in range(world)]
+    pendings = [b_next.clone() if r == 0 else torch.full((k, n), -1.0) for r in range(world)]
+    sent = [0] * world
+
+    def copier(rank):
+        def copy(dst, src, nbytes, stream):
+            sent[rank] += nbytes
+            ctypes.memmove(dst, src, nbytes)
+        return copy
+
+    handles = [_FakeHandle(currents), _FakeHandle(pendings)]
+    pipes = [CopyEngineBroadcast(currents[r], pendings[r], object(), handles, copy=copier(r),
+                                 new_stream=_FakeStream, world=world, rank=r) for r in range(world)]
+    parts = broadcast_parts(k, world)
+    assert parts[0][0] == 0 and parts[-1][1] == k and len(parts) == min(world - 1, k)
+    for pipe in pipes:
+        pipe.scatter()
+    for pipe in pipes:
+        pipe.forward()
+    for r in range(world):
+        assert torch.equal(pendings[r], b_next), r
+        assert torch.all(currents[r] == 7.0)
+    assert sent[0] == k * n * 4
