@@ -18,12 +18,14 @@ Metric: device-timed TFLOP/s = 2*M*K*N / t (the reference's src/main.py:102).
   end-to-end figure through the public API with host buffers.
 * N > 1 (default workload ``rowshard32768``): M=K=N=32768 BF16, U[-1,1), A and C
   row-sharded over the ranks; every step broadcasts one B from rank 0 (posted
-  one step ahead on its own communicator, overlapping the GEMMs) and gathers C
-  on rank 0 (``--gather root``, the default: the single-GPU call's result, on
-  one device) or on every rank (``--gather all``) in row chunks that overlap
-  the next chunk's GEMM, with ``--reserve-sms`` SMs left to the NCCL kernels;
-  one process per GPU under torchrun; time = max over ranks.  The other gather
-  variant, each part of a step alone and T1 are timed in the same run.
+  one step ahead, overlapping the GEMMs: by copy engines over symmetric memory,
+  ``--broadcast ce``, the default, or by NCCL on its own communicator) and
+  gathers C on rank 0 (``--gather root``, the default: the single-GPU call's
+  result, on one device) or on every rank (``--gather all``) in row chunks that
+  overlap the next chunk's GEMM, with ``--reserve-sms`` SMs left to the NCCL
+  kernels (2 with the copy-engine broadcast, 8 with NCCL's); one process per
+  GPU under torchrun; time = max over ranks.  The other gather variant, each
+  part of a step alone and T1 are timed in the same run.
 * ``--impl reference`` times the reference's CPU path (numpy FP32 GEMM,
   src/benchmark_backends.py:223-226) on the host cores over row slabs of the
   same workload; under torchrun only rank 0 runs it.
@@ -474,8 +476,9 @@ def single_gpu(args) -> dict:
 def multi_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
     """Row-sharded 32768^3 BF16 GEMM over `world` ranks (one process per GPU).
 
-    A step: broadcast of the next step's B (NCCL, own communicator, one step
-    ahead), the local rows' GEMMs in row chunks, and the C gather of every chunk
+    A step: broadcast of the next step's B, one step ahead (``--broadcast ce``:
+    copy-engine pushes over symmetric memory, ``sharded.CopyEngineBroadcast``;
+    ``nccl``: NCCL on its own communicator), the local rows' GEMMs in row chunks, and the C gather of every chunk
     as soon as it is done, to rank 0 (``--gather root``) or to every rank
     (``--gather all``) -- by copy-engine pushes into the peers' C (``--exchange
     ce``, no SM taken from the GEMM), by this library's push kernel (``push``) or
@@ -746,8 +749,9 @@ def multi_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic: U[-1,1) from fixed seeds, rounded to BF16",
         "config": {"workload": f"rowshard_bf16_{m}x{k}x{n}", "m": m, "k": k, "n": n, "precision": "bf16",
-                   "parallelism": f"row-sharded A/C over {world} ranks; every step broadcasts one B (NCCL, own "
-                                  f"communicator, posted one step ahead and overlapping the GEMMs) and "
+                   "parallelism": f"row-sharded A/C over {world} ranks; every step broadcasts one B ("
+                                  + ("copy engines" if args.broadcast == "ce" else "NCCL, own communicator")
+                                  + ", posted one step ahead and overlapping the GEMMs) and "
                                   + ("gathers C on rank 0" if args.gather == "root" else "all-gathers C")
                                   + f" in {plan.chunk_count} row chunks, each chunk's exchange overlapping the "
                                   f"next chunk's GEMM",
@@ -798,13 +802,15 @@ def main() -> int:
     parser.add_argument("--workload", choices=("square8192", "rowshard32768"), default=None)
     parser.add_argument("--size", type=int, default=None, help="override the sharded problem size")
     parser.add_argument("--chunks", type=int, default=8)
-    parser.add_argument("--reserve-sms", type=int, default=8,
-                        help="multi-GPU: SMs left free of GEMM CTAs for the NCCL kernels that overlap them")
+    parser.add_argument("--reserve-sms", type=int, default=None,
+                        help="multi-GPU: SMs left free of GEMM CTAs for the NCCL kernels that overlap them "
+                             "(default 2 with --broadcast ce, whose only kernels are one-element all-reduces; "
+                             "8 with --broadcast nccl)")
     parser.add_argument("--exchange", choices=("ce", "push", "nccl"), default="ce",
                         help="multi-GPU C exchange: copy-engine pushes over symmetric memory, this library's "
                              "push kernel over symmetric memory, or NCCL send/recv")
     parser.add_argument("--push-ctas", type=int, default=16, help="CTAs of the push kernel (--exchange push)")
-    parser.add_argument("--broadcast", choices=("nccl", "ce"), default="nccl",
+    parser.add_argument("--broadcast", choices=("nccl", "ce"), default="ce",
                         help="multi-GPU B broadcast: NCCL on its own communicator, or copy-engine pushes over "
                              "symmetric memory (rank 0 scatters B's parts, their owners forward them)")
     parser.add_argument("--gather", choices=("root", "all"), default="root",
@@ -826,6 +832,8 @@ def main() -> int:
     args = parser.parse_args()
     if args.warmup < 3:
         parser.error("at least 3 warm-up steps")
+    if args.reserve_sms is None:
+        args.reserve_sms = 2 if args.broadcast == "ce" else 8
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
