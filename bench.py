@@ -659,7 +659,9 @@ def multi_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
                                                "max": round(float(table[:, i].max()), 3)}
                                         for i, (name, _) in enumerate(marks)},
                  "marks": "gemm<i>: chunk i's GEMM done; exchange: this rank's pushes done; broadcast: the "
-                          "next step's B arrived; end: the step's last operation on the compute stream"}
+                          + ("this rank's copy-engine pushes of the next B done (the B is whole on every rank "
+                             "at the max over ranks)" if args.broadcast == "ce" else "next step's B arrived")
+                          + "; end: the step's last operation on the compute stream"}
 
     # FP64 check of rows received from a peer (its A shard is regenerated here
     # from the same seed): the GEMM and the exchange together.  All-gather: each

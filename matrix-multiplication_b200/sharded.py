@@ -4,25 +4,26 @@ The reference is single-device (src/benchmark_backends.py selects one
 ``--device``); this module is the multi-GPU layer of the B200 backend:
 
 * rank r owns rows ``shard_rows(M, P, r)`` of A and C (contiguous row blocks);
-* B (K x N) lives on rank 0 and is broadcast to every rank (NCCL over NVLink);
+* B (K x N) lives on rank 0 and is broadcast to every rank over NVLink;
 * each rank computes its C rows with the library's tcgen05 GEMM, one row
   chunk at a time, and every finished chunk is exchanged with grouped
   point-to-point transfers straight into each peer's full C (all-gather) or
   into rank 0's C only (gather to root), so the exchange of chunk i overlaps
   the GEMM of chunk i+1.  No kernel reads peer memory;
-* with ``BroadcastPipeline`` the B broadcast runs on its own communicator one
-  step ahead (double-buffered B), so it too overlaps the GEMMs; the GEMMs are
-  then launched on fewer SMs than the device has (``matmul_set_sm_limit``) so
-  that the communication kernels find free SMs while they run;
-  ``CopyEngineBroadcast`` does the same broadcast with copy-engine pushes over
+* the B broadcast runs one step ahead (double-buffered B), so it too overlaps
+  the GEMMs.  ``CopyEngineBroadcast`` does it with copy-engine pushes over
   symmetric memory (rank 0 scatters B's parts, their owners forward them), so
-  only two one-element all-reduces per step need an SM;
+  only two one-element all-reduces per step need an SM; ``BroadcastPipeline``
+  does it with NCCL on its own communicator, whose kernels need SMs for the
+  whole transfer.  Either way the GEMMs are launched on fewer SMs than the
+  device has (``matmul_set_sm_limit``) so that the communication kernels find
+  free SMs while they run;
 * with ``CopyEngineGather`` the C exchange takes no SM at all: C lives in
   symmetric memory (every rank maps every peer's C), and each finished chunk
   is pushed into the peers' C by copy-engine transfers (one cudaMemcpyAsync per
-  peer, on one stream per peer, so the copies of a chunk run side by side); a
-  one-element NCCL all-reduce at the end of the step completes only when every
-  rank's pushes are done, which makes the gathered C safe to read.
+  peer, peers visited in the order rank + 1, rank + 2, ... on one copy stream by
+  default); a one-element NCCL all-reduce at the end of the step completes only
+  when every rank's pushes are done, which makes the gathered C safe to read.
 
 Collectives are issued through ``torch.distributed`` (one process per GPU);
 the host-side plan (row ranges, chunking, peer lists) is independent of the
@@ -371,7 +372,10 @@ def pipelined_step_ce(plan: ShardPlan, a_local: torch.Tensor, pipe: BroadcastPip
 
     With ``marks`` (a list), timing events are appended as (name, event) pairs:
     "start", "gemm<i>" after chunk i's GEMM, "exchange" when this rank's pushes
-    are done, "broadcast" when the next B has arrived, "end" after the step.
+    are done, "broadcast" when ``pipe.join`` returns (NCCL: the next B has
+    arrived here; ``CopyEngineBroadcast``: this rank's pushes of it are done, so
+    the B is whole everywhere at the latest of these over the ranks), "end"
+    after the step.
     """
     if marks is not None:
         marks.append(("start", _timing_event()))
