@@ -794,7 +794,9 @@ def multi_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
     }
 
 
-def main() -> int:
+def parse_args(argv: list[str] | None = None) -> argparse.Namespace:
+    """Command line -> arguments, with the defaults that depend on other flags resolved
+    (``--reserve-sms``, ``--workload``, ``--steps``)."""
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=None,
@@ -831,18 +833,25 @@ def main() -> int:
                              "4096^3 and 8192^3 as comparison rows")
     parser.add_argument("--cases", nargs="+", default=None, metavar="MxKxN:PREC[:normal]",
                         help="like --sweep, for the listed shapes (inputs U[-1,1), or N(0, 1/sqrt(K)) with :normal)")
-    args = parser.parse_args()
+    args = parser.parse_args(argv)
     if args.warmup < 3:
         parser.error("at least 3 warm-up steps")
     if args.reserve_sms is None:
         args.reserve_sms = 2 if args.broadcast == "ce" else 8
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.workload is None:
         args.workload = "square8192" if args.gpus == 1 else "rowshard32768"
     if args.steps is None:
         args.steps = 21 if args.workload == "square8192" else 20
+    args.parser = parser
+    return args
+
+
+def main() -> int:
+    args = parse_args()
+    parser = args.parser
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.sweep == "legacy":
         legacy_sweep()
         return 0

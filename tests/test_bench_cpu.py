@@ -75,3 +75,17 @@ def test_case_parser():
     for bad in ("4096x4096:bf16", "4096x4096x4096:int8", "0x1x1:fp32", "1x1x1:fp16:gaussian", "1x1x1"):
         with pytest.raises(SystemExit):
             bench.parse_case(bad)
+
+
+def test_multi_gpu_defaults():
+    """The driver's multi-GPU command uses the copy-engine broadcast with 2 SMs left
+    to the one-element all-reduces; the NCCL broadcast keeps 8 for its kernels;
+    an explicit --reserve-sms wins."""
+    args = bench.parse_args(["--gpus", "8"])
+    assert (args.broadcast, args.exchange, args.gather) == ("ce", "ce", "root")
+    assert args.reserve_sms == 2
+    assert args.workload == "rowshard32768" and args.steps == 20
+    assert bench.parse_args(["--gpus", "8", "--broadcast", "nccl"]).reserve_sms == 8
+    assert bench.parse_args(["--gpus", "8", "--reserve-sms", "0"]).reserve_sms == 0
+    single = bench.parse_args([])
+    assert single.workload == "square8192" and single.steps == 21 and single.warmup == 10
