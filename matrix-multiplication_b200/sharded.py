@@ -262,6 +262,12 @@ class CopyEngineBroadcast:
         if self.world > 1:
             self.join()
             dist.all_reduce(self.token, group=self.group)
+        self.swap()
+
+    def swap(self) -> None:
+        """The buffer just filled becomes ``current``; the one computed with until
+        now becomes ``pending`` (and its peers' mappings the target of the next
+        pushes).  ``finish`` calls it once every rank's pushes are done."""
         self.which ^= 1
         self.current, self.pending = self.local[self.which ^ 1], self.local[self.which]
 

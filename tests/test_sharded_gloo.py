@@ -284,3 +284,33 @@ def test_copy_engine_broadcast_delivers_b_to_every_rank(world, k):
         assert torch.equal(pendings[r], b_next), r
         assert torch.all(currents[r] == 7.0)
     assert sent[0] == k * n * 4
+
+
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_copy_engine_broadcast_alternates_buffers_over_steps(world):
+    """Three steps, each with a different B on rank 0: after every step's pushes and
+    swap, every rank computes with that step's B, and the buffer the pushes wrote
+    was never the one a rank was computing with during the step."""
+    import ctypes
+
+    from sharded import CopyEngineBroadcast
+
+    k, n = 11, 3
+    first = [torch.full((k, n), 1.0) for _ in range(world)]
+    second = [torch.full((k, n), -1.0) for _ in range(world)]
+    handles = [_FakeHandle(first), _FakeHandle(second)]
+    pipes = [CopyEngineBroadcast(first[r], second[r], object(), handles, copy=_memmove_copy,
+                                 new_stream=_FakeStream, world=world, rank=r) for r in range(world)]
+    for step in range(3):
+        b_next = torch.arange(k * n, dtype=torch.float32).reshape(k, n) + 100.0 * (step + 1)
+        pipes[0].pending.copy_(b_next)                 # rank 0: the next step's B
+        in_use = [pipe.current.clone() for pipe in pipes]
+        for pipe in pipes:
+            pipe.scatter()
+        for pipe in pipes:
+            pipe.forward()
+        for r, pipe in enumerate(pipes):
+            assert torch.equal(pipe.current, in_use[r]), (step, r)   # not written while computed with
+            pipe.swap()
+            assert torch.equal(pipe.current, b_next), (step, r)
+            assert pipe.pending.data_ptr() != pipe.current.data_ptr()
